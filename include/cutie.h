@@ -1,0 +1,158 @@
+/*
+ * cutie.h — C ABI of the B200 (sm_100a) residual-add + RMSNorm + FP8 (e4m3)
+ * activation-quantization path.
+ *
+ * Every entry point is destination-passing: the caller owns and preallocates
+ * all device buffers, nothing is allocated inside, and the work is enqueued
+ * asynchronously on the caller's CUDA stream (`stream` is a cudaStream_t; NULL
+ * means the legacy default stream) on the calling thread's current device.
+ * No C++ exception crosses this boundary: every function returns a status code
+ * (CUTIE_OK == 0) and, on failure, a message readable through
+ * cutie_last_error() on the same thread.
+ *
+ * Reference interfaces replaced (paths within the S1ro1/thingy project):
+ *   cutie_rms_norm_fp8          <- RMSNorm.__call__ / rms_norm_kernel
+ *                                  (src/cutie/rms_norm/rms_norm.py:50-311),
+ *                                  compiled and bound through cute.compile at
+ *                                  src/cutie/rms_norm/bench.py:278-301, and the
+ *                                  functional reference it must agree with,
+ *                                  residual_rms_norm_fp8_reference
+ *                                  (src/cutie/rms_norm/bench.py:83-100).
+ *   cutie_per_token_cast_to_fp8 <- per_token_cast_to_fp8_triton /
+ *                                  _per_token_fp8_kernel
+ *                                  (src/cutie/vendor/prime_rl/fp8_utils.py:21-89),
+ *                                  the op behind the custom op
+ *                                  cutie::per_token_fp8_quant
+ *                                  (src/cutie/rms_norm/bench.py:68-80).
+ *   cutie_rms_norm              <- rms_norm / rms_norm_on_stream
+ *                                  (src/cutie/rms_norm/rms_norm.py:11-33, fp32)
+ *                                  and rms_norm_reference
+ *                                  (src/cutie/rms_norm/bench.py:58-65, bf16).
+ */
+#ifndef CUTIE_H_
+#define CUTIE_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CUTIE_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define CUTIE_API __attribute__((visibility("default")))
+#else
+#define CUTIE_API
+#endif
+
+/* ---- status codes ------------------------------------------------------- */
+enum cutie_status {
+  CUTIE_OK = 0,
+  CUTIE_ERR_INVALID_ARGUMENT = -1, /* bad shape, null pointer, bad enum      */
+  CUTIE_ERR_UNSUPPORTED = -2,      /* valid request this build cannot serve  */
+  CUTIE_ERR_ALIGNMENT = -3,        /* pointer / leading dim not 16-B aligned */
+  CUTIE_ERR_CUDA = -4,             /* a CUDA runtime call failed             */
+};
+
+/* ---- quantization granularity (who shares one scale) -------------------- */
+enum cutie_quant_mode {
+  CUTIE_QUANT_NONE = 0,  /* no FP8 output (plain RMSNorm)                    */
+  CUTIE_QUANT_TOKEN = 1, /* one scale per row (group = H)                    */
+  CUTIE_QUANT_GROUP = 2, /* one scale per `group_size` contiguous elements   */
+};
+
+/* ---- how a scale is encoded --------------------------------------------- */
+enum cutie_scale_fmt {
+  CUTIE_SCALE_FP32 = 0,      /* fp32 s = max(amax/448, 1e-4)                 */
+  CUTIE_SCALE_FP32_POW2 = 1, /* fp32 s = 2^ceil(log2(max(amax/448, 1e-4)))   */
+                             /* (the reference's use_ue8m0=True rule)        */
+  CUTIE_SCALE_E8M0 = 2,      /* one byte: biased exponent of the POW2 scale  */
+};
+
+/* ---- where scale (row m, group g) lives --------------------------------- */
+enum cutie_scale_layout {
+  CUTIE_LAYOUT_ROW_MAJOR = 0,   /* scale[m * ld_scale + g], ld >= n_groups   */
+  CUTIE_LAYOUT_COL_MAJOR = 1,   /* scale[g * ld_scale + m], ld >= M          */
+  CUTIE_LAYOUT_MX_SWIZZLED = 2, /* Blackwell block-scaled-GEMM layout:       */
+  /* 128x4 tiles of 512 bytes, tile (m/128, g/4) at ((m/128)*ceil(G/4)+g/4)*512,
+   * inside a tile (m%32)*16 + ((m%128)/32)*4 + g%4. Rows are padded to a
+   * multiple of 128 and groups to a multiple of 4; padding bytes are written
+   * as 0. Requires CUTIE_SCALE_E8M0. ld_scale is ignored.                   */
+};
+
+/* ---- element types for cutie_rms_norm ----------------------------------- */
+enum cutie_dtype {
+  CUTIE_DTYPE_BF16 = 0,
+  CUTIE_DTYPE_F32 = 1,
+};
+
+/*
+ * Fused [residual add] -> RMSNorm -> [FP8 e4m3 quantization].
+ *
+ *   r   = bf16(x + residual)                (or r = x when residual is NULL)
+ *   inv = 1 / RN(sqrt(RN(sum(r^2) / H) + eps))            (fp32 statistics)
+ *   n   = bf16( bf16(r * inv) * weight )    (cast before the weight multiply)
+ *   per group: amax = max|n|, s = max(amax / 448, 1e-4) [, rounded up to 2^k]
+ *   q   = e4m3_rne(RN(n / s))
+ *
+ * x, residual, weight, residual_out, normalized_out: bf16. q: e4m3 bytes.
+ * M >= 0 rows, H > 0 columns, H % 8 == 0; in CUTIE_QUANT_GROUP mode
+ * group_size is 32, 64 or 128 and the last group of a row may be partial
+ * (n_groups = ceil(H / group_size)). Leading dimensions are in elements; every
+ * row must start 16-byte aligned. residual_out / normalized_out may be NULL
+ * (not written); residual_out requires residual. q and scale may be NULL only
+ * when quant_mode == CUTIE_QUANT_NONE. ld_scale == 0 selects the dense leading
+ * dimension (n_groups for row-major, M for column-major).
+ * threads_per_row: 0 picks the launch shape; otherwise a multiple of 32 in
+ * [32, 1024] that must cover the row with at most 8 16-byte vectors a thread.
+ */
+CUTIE_API int cutie_rms_norm_fp8(const void* x, int64_t ldx,
+                       const void* residual, int64_t ldr,
+                       const void* weight, float eps,
+                       int64_t M, int64_t H,
+                       int quant_mode, int group_size,
+                       int scale_fmt, int scale_layout, int64_t ld_scale,
+                       void* q, int64_t ldq, void* scale,
+                       void* residual_out, int64_t ldro,
+                       void* normalized_out, int64_t ldn,
+                       int threads_per_row, void* stream);
+
+/*
+ * Quantization alone: bf16 x [M, H] -> e4m3 q [M, H] + scales, one scale per
+ * (row, group). Same scale rules, formats and layouts as above; group_size 0
+ * means one scale per row. Mirrors per_token_cast_to_fp8_triton(x, use_ue8m0,
+ * gran_k) (src/cutie/vendor/prime_rl/fp8_utils.py:63-89), whose defaults are
+ * group_size 128, CUTIE_SCALE_FP32 (use_ue8m0=False) or CUTIE_SCALE_FP32_POW2
+ * (use_ue8m0=True), row-major [M, ceil(H/128)] scales.
+ */
+CUTIE_API int cutie_per_token_cast_to_fp8(const void* x, int64_t ldx,
+                                int64_t M, int64_t H, int group_size,
+                                int scale_fmt, int scale_layout,
+                                int64_t ld_scale,
+                                void* q, int64_t ldq, void* scale,
+                                int threads_per_row, void* stream);
+
+/*
+ * Standalone RMSNorm, out = f(x) [M, H].
+ *   dtype == CUTIE_DTYPE_BF16: out = bf16(bf16(x * inv) * w), inv as above
+ *     (rms_norm_reference, src/cutie/rms_norm/bench.py:58-65).
+ *   dtype == CUTIE_DTYPE_F32:  out = RN(RN(x / RN(sqrt(RN(mean(RN(x^2))) + eps))) * w)
+ *     (rms_norm, src/cutie/rms_norm/rms_norm.py:11-20).
+ * x, weight and out share `dtype`. H % 8 == 0 (bf16) or H % 4 == 0 (f32).
+ */
+CUTIE_API int cutie_rms_norm(const void* x, int64_t ldx, const void* weight, float eps,
+                   int64_t M, int64_t H, int dtype,
+                   void* out, int64_t ldo, int threads_per_row, void* stream);
+
+/* Message of the last failing call on this thread ("" if none). */
+CUTIE_API const char* cutie_last_error(void);
+
+/* CUTIE_ABI_VERSION of the loaded library. */
+CUTIE_API int cutie_abi_version(void);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CUTIE_H_ */

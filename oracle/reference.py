@@ -1,0 +1,142 @@
+"""CPU oracle of the fused RMSNorm -> FP8 path.  TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline legs may
+import this module, and only as the checker or the timed CPU baseline; the
+product path (thingy_b200) never calls it.
+
+It restates the reference's own PyTorch path with the same torch CPU ops:
+  rms_norm_reference     src/cutie/rms_norm/bench.py:58-65
+  residual add           src/cutie/rms_norm/bench.py:97
+  group quantization     src/cutie/vendor/prime_rl/fp8_utils.py:38-60
+                         (the Triton kernel's tensor math: masked load with
+                         other=0.0 :45-49, amax :50, clamp :51, UE8M0 :52-53,
+                         divide :54, e4m3 cast :57)
+  fp32 rms_norm          src/cutie/rms_norm/rms_norm.py:11-20 (eager form)
+generalised to one scale per row (group = H), 1x32 / 1x64 groups and e8m0
+bytes, which the reference does not implement (its quantizer asserts
+gran_k == 128, fp8_utils.py:67).
+
+Pinning: tests/golden/ holds vectors produced by importing the reference's
+own functions (bench.py's rms_norm_reference and residual path, and the
+vendored Triton kernel run by Triton's CPU interpreter); tests check this
+oracle against them. The interpreter mis-rounds e4m3 when rounding carries
+into the next binade; those elements are recorded and checked separately.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+E4M3_MAX = 448.0
+MIN_SCALE = 1e-4
+
+
+def residual_add(x: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+    """bench.py:97 — bf16 + bf16 (fp32 sum rounded to bf16)."""
+    return x + residual
+
+
+def rms_norm_reference(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6) -> torch.Tensor:
+    """bench.py:58-65 — fp32 statistics, cast to x.dtype before the weight multiply."""
+    x_f32 = x.float()
+    variance = x_f32.square().mean(dim=-1, keepdim=True)
+    normalized = x_f32 * torch.rsqrt(variance + eps)
+    return normalized.to(x.dtype) * weight
+
+
+def rms_norm_f32(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
+    """rms_norm.py:11-20 — the standalone fp32 RMSNorm, evaluated eagerly."""
+    variance = x.pow(2).mean(dim=-1, keepdim=True) + eps
+    x = x / torch.sqrt(variance)
+    return x * weight
+
+
+def pow2_ceil(scale: torch.Tensor) -> torch.Tensor:
+    """fp8_utils.py:52-53 — 2^ceil(log2 s), computed exactly from the bits.
+
+    For positive normal fp32 s this equals exp2(ceil(log2(s))) whenever log2
+    is exact on powers of two and distinguishes non-powers; the bit form has
+    no such caveat. tests/test_oracle.py checks both agree on the inputs used.
+    """
+    bits = scale.contiguous().view(torch.int32)
+    exp = bits & 0x7F800000
+    bumped = torch.where((bits & 0x007FFFFF) != 0, exp + 0x00800000, exp)
+    return bumped.view(torch.float32)
+
+
+def quantize(
+    n: torch.Tensor, group_size: int | None = 128, scale_format: str = "fp32"
+) -> tuple[torch.Tensor, torch.Tensor]:
+    """Per-(row, group) FP8 e4m3 quantization of n [M, H].
+
+    group_size None means one group per row. Returns (q as uint8 codes [M, H],
+    scale [M, G]): fp32 for "fp32" / "ue8m0", uint8 biased exponents for
+    "e8m0". A partial last group is padded with zeros, as the Triton kernel's
+    masked load (other=0.0) does.
+    """
+    M, H = n.shape
+    gs = H if not group_size else group_size
+    G = -(-H // gs)
+    xf = n.float()
+    if G * gs != H:
+        xf = torch.nn.functional.pad(xf, (0, G * gs - H))
+    xg = xf.view(M, G, gs)
+    amax = xg.abs().amax(dim=-1)
+    scale = torch.clamp(amax / E4M3_MAX, min=MIN_SCALE)
+    if scale_format in ("ue8m0", "e8m0"):
+        scale = pow2_ceil(scale)
+    y = xg / scale[..., None]
+    q = y.to(torch.float8_e4m3fn).view(torch.uint8).view(M, G * gs)[:, :H].contiguous()
+    if scale_format == "e8m0":
+        scale = ((scale.view(torch.int32) >> 23) & 0xFF).to(torch.uint8)
+    return q, scale
+
+
+def rms_norm_fp8(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float = 1e-6,
+    residual: torch.Tensor | None = None,
+    group_size: int | None = 128,
+    scale_format: str = "fp32",
+):
+    """[residual add] -> rms_norm_reference -> quantize (bench.py:83-100 generalised).
+
+    Returns (q uint8 [M, H], scale [M, G], residual_out or None, normalized).
+    """
+    r = residual_add(x, residual) if residual is not None else x
+    n = rms_norm_reference(r, weight, eps)
+    q, s = quantize(n, group_size, scale_format)
+    return q, s, (r if residual is not None else None), n
+
+
+def mx_swizzle(scales: np.ndarray) -> np.ndarray:
+    """[M, G] e8m0 bytes -> flat Blackwell block-scaled layout (zero padded).
+
+    Restated from the public cuBLAS / PTX description of the 1D block
+    scaling-factor layout: 128x4 tiles, 512 bytes each, tile-row-major;
+    inside a tile row r, column c at (r % 32) * 16 + (r // 32) * 4 + c.
+    Written independently of thingy_b200.layouts (which the kernel mirrors).
+    """
+    M, G = scales.shape
+    rows = -(-M // 128) * 128
+    cols = -(-G // 4) * 4
+    padded = np.zeros((rows, cols), dtype=np.uint8)
+    padded[:M, :G] = scales
+    # tile view [row_tile, 128, col_tile, 4] -> [row_tile, col_tile, 4 (r//32), 32 (r%32), 4 (c)]
+    t = padded.reshape(rows // 128, 4, 32, cols // 4, 4)  # r = 32*a + b
+    t = t.transpose(0, 3, 2, 1, 4)  # [rt, ct, b (r%32), a (r//32), c]
+    return np.ascontiguousarray(t).reshape(-1)
+
+
+def layout_scales(scale: torch.Tensor, layout: str) -> np.ndarray:
+    """The device buffer contents for a [M, G] scale matrix in ``layout``."""
+    s = scale.numpy()
+    if layout == "row":
+        return s
+    if layout == "col":
+        return np.ascontiguousarray(s.T)
+    if layout == "mx":
+        return mx_swizzle(s)
+    raise ValueError(layout)

@@ -1,0 +1,151 @@
+"""Comparison helpers shared by the GPU parity tests (GPU output vs CPU oracle)."""
+
+from __future__ import annotations
+
+import numpy as np
+import torch
+
+from oracle import reference as ora
+from thingy_b200.layouts import mx_unswizzle, n_groups
+
+
+def bf16_bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def bf16_ulp_diff(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Distance in bf16 ulps between two bit patterns (monotone ordering)."""
+
+    def ordered(u):
+        u = u.astype(np.int32)
+        return np.where(u & 0x8000, -(u & 0x7FFF), u)
+
+    return np.abs(ordered(a) - ordered(b))
+
+
+def e4m3_ulp_diff(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """Distance in e4m3 codes (monotone ordering; +0 and -0 coincide)."""
+
+    def ordered(c):
+        c = c.astype(np.int32)
+        return np.where(c & 0x80, -(c & 0x7F), c)
+
+    return np.abs(ordered(a) - ordered(b))
+
+
+def q_codes(q: torch.Tensor) -> np.ndarray:
+    return q.detach().cpu().contiguous().view(torch.uint8).numpy()
+
+
+def scale_matrix(s: torch.Tensor, M: int, H: int, group_size, fmt: str, layout: str) -> np.ndarray:
+    """The GPU's scales as an [M, G] array (uint8 exponents for e8m0)."""
+    G = n_groups(H, group_size)
+    s = s.detach().cpu()
+    if fmt == "e8m0":
+        s = s.view(torch.uint8)
+    if layout == "mx":
+        return mx_unswizzle(s.numpy(), M, G)
+    if s.dim() == 1:
+        return s.numpy().reshape(M, G)
+    return s.contiguous().numpy().reshape(M, G)
+
+
+def gpu_run(inp: dict, group_size, fmt: str, layout: str, *, normalized=True, threads=0,
+            device="cuda"):
+    import thingy_b200 as tb
+
+    x = inp["x"].to(device)
+    w = inp["weight"].to(device)
+    res = inp.get("residual")
+    res = None if res is None else res.to(device)
+    q, s, r, n = tb.rms_norm_fp8(
+        x, w, inp["eps"], residual=res, group_size=group_size, scale_format=fmt,
+        scale_layout=layout, return_normalized=normalized, threads_per_row=threads,
+    )
+    torch.cuda.synchronize()
+    return q, s, r, n
+
+
+def check_parity(inp: dict, group_size, fmt: str, layout: str, *, exact: bool = False,
+                 threads: int = 0, budget: float = 1e-3) -> dict:
+    """Run GPU and oracle on the same inputs; assert the tolerance contract.
+
+    residual_out: bit-exact. normalized: at most 1 bf16 ulp on <= budget of
+    elements (fp32 sum order is the only difference). Quantization of the
+    GPU's own normalized output: bit-exact (scales and codes). End to end:
+    scales bit-exact wherever the group's normalized values agree, codes within
+    1 e4m3 ulp on <= budget of elements. exact=True: everything bit-exact.
+    """
+    M, H = inp["x"].shape
+    q, s, r, n = gpu_run(inp, group_size, fmt, layout, threads=threads)
+    q_ref, s_ref, r_ref, n_ref = ora.rms_norm_fp8(
+        inp["x"], inp["weight"], inp["eps"], residual=inp.get("residual"),
+        group_size=group_size, scale_format=fmt,
+    )
+    stats = {}
+    if r_ref is not None:
+        np.testing.assert_array_equal(bf16_bits(r), bf16_bits(r_ref))
+    nd = bf16_ulp_diff(bf16_bits(n), bf16_bits(n_ref))
+    stats["normalized_diff_frac"] = float((nd != 0).mean()) if nd.size else 0.0
+    if exact:
+        assert nd.max(initial=0) == 0, "normalized differs on exact-sum inputs"
+    else:
+        assert nd.max(initial=0) <= 1
+        assert stats["normalized_diff_frac"] <= budget
+    # quantization stage, fed the GPU's own normalized values: bit-exact
+    qc = q_codes(q)
+    sm = scale_matrix(s, M, H, group_size, fmt, layout)
+    q_own, s_own = ora.quantize(n.cpu(), group_size, fmt)
+    np.testing.assert_array_equal(sm, s_own.numpy())
+    np.testing.assert_array_equal(qc, q_own.numpy())
+    if layout == "mx":  # the whole buffer, zero padding included
+        np.testing.assert_array_equal(
+            s.detach().cpu().view(torch.uint8).numpy(), ora.layout_scales(s_own, "mx")
+        )
+    # end to end against the oracle
+    gs = H if not group_size else group_size
+    G = n_groups(H, group_size)
+    pad = G * gs - H
+    group_same = (np.pad(nd, ((0, 0), (0, pad))).reshape(M, G, gs) == 0).all(-1)
+    sr = s_ref.numpy()
+    np.testing.assert_array_equal(sm[group_same], sr[group_same])
+    qd = e4m3_ulp_diff(qc, q_ref.numpy())
+    stats["q_diff_frac"] = float((qd != 0).mean()) if qd.size else 0.0
+    if exact:
+        np.testing.assert_array_equal(sm, sr)
+        assert qd.max(initial=0) == 0, "codes differ on exact-sum inputs"
+    else:
+        if fmt == "fp32" and (~group_same).any():
+            rel = np.abs(sm[~group_same] - sr[~group_same]) / sr[~group_same]
+            assert rel.max() <= 2.0**-7, "scale moved by more than one bf16 ulp of amax"
+        assert qd.max(initial=0) <= 1
+        assert stats["q_diff_frac"] <= budget
+    return stats
+
+
+def exact_sum_inputs(M: int, H: int, *, residual: bool, seed: int = 0) -> dict:
+    """Inputs whose fp32 sum of squares is exact in any order.
+
+    x (and residual) are k/16 with small integers k, so every square is a
+    multiple of 2^-8 and every partial sum over H <= 8192 elements stays below
+    2^15: 23 significant bits, exact in fp32. Any summation order gives the
+    oracle's bits, so every output can be compared bit for bit.
+    """
+    g = torch.Generator().manual_seed(seed)
+    lim = 16 if residual else 32
+    x = (torch.randint(-lim, lim + 1, (M, H), generator=g).float() / 16).to(torch.bfloat16)
+    w = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    out = {"x": x, "weight": w, "eps": 1e-6}
+    if residual:
+        out["residual"] = (torch.randint(-16, 17, (M, H), generator=g).float() / 16).to(torch.bfloat16)
+    return out
+
+
+def random_inputs(M: int, H: int, *, residual: bool, seed: int = 0, eps: float = 1e-6) -> dict:
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(M, H, generator=g).to(torch.bfloat16)
+    w = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16)
+    out = {"x": x, "weight": w, "eps": eps}
+    if residual:
+        out["residual"] = (2.0 * torch.randn(M, H, generator=g)).to(torch.bfloat16)
+    return out

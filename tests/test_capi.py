@@ -1,0 +1,97 @@
+"""The C ABI library loads, exports every declared symbol, and rejects bad
+arguments with status codes before touching CUDA (no GPU needed)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+
+from thingy_b200 import _lib
+
+HEADER = Path(__file__).resolve().parent.parent / "include" / "cutie.h"
+
+
+@pytest.fixture(scope="module")
+def lib():
+    if not _lib.library_path().exists():
+        from thingy_b200.build import build
+
+        build()
+    return _lib.load()
+
+
+def declared_symbols() -> list[str]:
+    text = HEADER.read_text()
+    return re.findall(r"CUTIE_API\s+(?:const\s+)?\w+\s*\*?\s*(cutie_\w+)\s*\(", text)
+
+
+def test_header_declares_the_binding_table():
+    assert sorted(declared_symbols()) == sorted(_lib.EXPORTED_SYMBOLS)
+
+
+def test_exports_every_declared_symbol(lib):
+    for name in declared_symbols():
+        assert hasattr(lib, name), name
+    assert lib.cutie_abi_version() == _lib.ABI_VERSION
+
+
+def test_exports_nothing_else():
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.library_path())],
+                         capture_output=True, text=True, check=True).stdout
+    names = {line.split()[-1] for line in out.splitlines() if " T " in line}
+    assert {n for n in names if n.startswith("cutie_")} == set(_lib.EXPORTED_SYMBOLS)
+
+
+FAKE = ctypes.c_void_p(0x10000)  # never dereferenced: every call below fails validation
+
+
+def fused(lib, **kw):
+    args = dict(x=FAKE, ldx=1024, residual=None, ldr=0, weight=FAKE, eps=1e-6, M=4, H=1024,
+                quant_mode=_lib.QUANT_GROUP, group_size=128, scale_fmt=0, scale_layout=0,
+                ld_scale=0, q=FAKE, ldq=1024, scale=FAKE, residual_out=None, ldro=0,
+                normalized_out=None, ldn=0, threads_per_row=0, stream=None)
+    args.update(kw)
+    return lib.cutie_rms_norm_fp8(*args.values())
+
+
+@pytest.mark.parametrize(
+    "kw,code,needle",
+    [
+        ({"M": -1}, _lib.ERR_INVALID_ARGUMENT, "M >= 0"),
+        ({"H": 0}, _lib.ERR_INVALID_ARGUMENT, "H > 0"),
+        ({"H": 1020, "ldx": 1020, "ldq": 1020}, _lib.ERR_UNSUPPORTED, "multiple of 8"),
+        ({"quant_mode": 9}, _lib.ERR_INVALID_ARGUMENT, "quant_mode"),
+        ({"group_size": 48}, _lib.ERR_UNSUPPORTED, "group_size"),
+        ({"scale_fmt": 5}, _lib.ERR_INVALID_ARGUMENT, "scale_fmt"),
+        ({"scale_layout": 5}, _lib.ERR_INVALID_ARGUMENT, "scale_layout"),
+        ({"residual_out": FAKE, "ldro": 1024}, _lib.ERR_INVALID_ARGUMENT, "requires residual"),
+        ({"quant_mode": 0}, _lib.ERR_INVALID_ARGUMENT, "no output"),
+        ({"scale_layout": 2}, _lib.ERR_INVALID_ARGUMENT, "E8M0"),
+        ({"eps": float("nan")}, _lib.ERR_INVALID_ARGUMENT, "eps"),
+    ],
+)
+def test_argument_errors(lib, kw, code, needle):
+    assert fused(lib, **kw) == code
+    assert needle in lib.cutie_last_error().decode()
+
+
+def test_empty_batch_is_a_no_op(lib):
+    assert fused(lib, M=0, x=None, q=None, scale=None, weight=None) == _lib.OK
+    assert lib.cutie_last_error() == b""
+
+
+def test_quantizer_and_rms_norm_errors(lib):
+    assert lib.cutie_per_token_cast_to_fp8(FAKE, 1024, 4, 1024, 48, 0, 0, 0, FAKE, 1024, FAKE,
+                                           0, None) == _lib.ERR_UNSUPPORTED
+    assert lib.cutie_rms_norm(FAKE, 1024, FAKE, 1e-5, 4, 1024, 7, FAKE, 1024, 0, None) == \
+        _lib.ERR_INVALID_ARGUMENT
+    assert lib.cutie_rms_norm(FAKE, 1024, FAKE, 1e-5, 4, 1022, _lib.DTYPE_F32, FAKE, 1024, 0,
+                              None) == _lib.ERR_UNSUPPORTED
+
+
+def test_python_maps_status_to_exceptions(lib):
+    with pytest.raises(ValueError, match="multiple of 8"):
+        _lib.check(fused(lib, H=1020, ldx=1020, ldq=1020))

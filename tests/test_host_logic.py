@@ -1,0 +1,105 @@
+"""Host-side logic that needs no GPU: layouts, workloads, sharding, API validation."""
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import reference as ora
+import thingy_b200 as tb
+from thingy_b200 import layouts
+from thingy_b200.rms_norm import _threads_hint
+from thingy_b200.shard import all_shards, shard_rows
+from thingy_b200.workloads import WORKLOADS, make_inputs
+
+
+def test_swizzle_two_implementations_agree():
+    rng = np.random.default_rng(0)
+    for M, G in [(1, 160), (8, 160), (128, 160), (130, 36), (300, 3), (5, 1)]:
+        a = rng.integers(0, 256, (M, G), dtype=np.uint8)
+        got = layouts.mx_swizzle(a)
+        np.testing.assert_array_equal(got, ora.mx_swizzle(a))
+        np.testing.assert_array_equal(layouts.mx_unswizzle(got, M, G), a)
+        assert got.size == layouts.mx_swizzled_size(M, G)
+
+
+def test_swizzle_known_positions():
+    # inside one 128x4 tile: rows 0,32,64,96 of column c share a 16-byte line
+    off = layouts.mx_swizzle_offset
+    assert off(0, 0, 4) == 0 and off(0, 3, 4) == 3
+    assert off(32, 0, 4) == 4 and off(64, 0, 4) == 8 and off(96, 1, 4) == 13
+    assert off(1, 0, 4) == 16 and off(31, 2, 4) == 31 * 16 + 2
+    # next column tile, next row tile
+    assert off(0, 4, 8) == 512 and off(128, 0, 8) == 2 * 512
+
+
+def test_workload_bytes_match_the_traffic_model():
+    assert WORKLOADS["token_4096x4096"].bytes_moved() == 50_356_224
+    assert WORKLOADS["g128_16384x7168"].bytes_moved() == 356_005_888
+    assert WORKLOADS["residual_token_32768x8192"].bytes_moved() == 1_879_195_648
+    assert [WORKLOADS["mx32_decode_5120"].bytes_moved(m) for m in (1, 8, 32, 128)] == [
+        25_760, 134_400, 506_880, 1_996_800]
+    assert WORKLOADS["g128_sharded_262144x8192"].bytes_moved() == 6_509_576_192
+
+
+def test_inputs_are_seeded_and_shaped():
+    w = WORKLOADS["g128_16384x7168"]
+    a = make_inputs(w, 64, seed=0)
+    b = make_inputs(w, 64, seed=0)
+    assert torch.equal(a["x"], b["x"]) and torch.equal(a["weight"], b["weight"])
+    assert a["x"].dtype == torch.bfloat16 and a["x"].shape == (64, 7168)
+    col_rms = a["x"].float().square().mean(0).sqrt()
+    assert int((col_rms > 10).sum()) == 7  # round(0.001 * 7168) outlier channels x50
+    r = make_inputs(WORKLOADS["residual_token_32768x8192"], 256, seed=0)
+    assert 1.8 < r["residual"].float().std().item() < 2.2
+    t = make_inputs(WORKLOADS["mx32_decode_5120"], 128, seed=0)["x"].float()
+    kurt = ((t - t.mean()) ** 4).mean() / t.var() ** 2
+    assert kurt > 4.0  # heavy tails of Student-t(4)
+
+
+def test_shard_rows_cover_everything_once():
+    for M in (0, 1, 7, 16384, 262144, 262147):
+        for world in (1, 2, 3, 4, 8):
+            shards = all_shards(M, world)
+            assert shards[0].start == 0 and shards[-1].stop == M
+            for a, b in zip(shards, shards[1:]):
+                assert a.stop == b.start
+            sizes = [s.rows for s in shards]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_rows(10, 2, 2)
+
+
+def test_python_api_rejects_cpu_tensors_without_touching_the_library():
+    x = torch.zeros(4, 1024, dtype=torch.bfloat16)
+    w = torch.ones(1024, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA"):
+        tb.rms_norm_fp8(x, w)
+    with pytest.raises(ValueError, match="CUDA"):
+        tb.rms_norm(x, w)
+
+
+def test_rmsnorm_knobs_validated_like_the_reference():
+    with pytest.raises(ValueError):
+        tb.RMSNorm(elements_per_thread=2, threads_per_row=128)
+    with pytest.raises(ValueError):
+        tb.RMSNorm(elements_per_thread=8, threads_per_row=100)
+    with pytest.raises(ValueError):
+        tb.RMSNorm(8, 128, load_path="tma")
+    with pytest.raises(ValueError):
+        tb.RMSNorm(8, 128, reduction="tree")
+    tb.RMSNorm(4, 256, "direct", "warp0")
+
+
+def test_threads_hint():
+    assert _threads_hint(None, 7168) == 0
+    assert _threads_hint(128, 7168) == 128  # 7 vectors a thread
+    assert _threads_hint(32, 7168) == 0     # 28 vectors a thread: library picks
+    assert _threads_hint(1024, 65536) == 0  # 8 vectors with 1024 threads: too many registers
+
+
+def test_empty_scale_shapes():
+    s = tb.empty_scale(10, 7168, 128, "fp32", "col")
+    assert s.shape == (10, 56) and s.stride() == (1, 10)
+    s = tb.empty_scale(10, 5120, 32, "e8m0", "mx")
+    assert s.numel() == 128 * 160 and s.element_size() == 1
+    assert tb.empty_scale(10, 4096, None).shape == (10, 1)

@@ -1,0 +1,324 @@
+// extern "C" entry points declared in include/cutie.h: argument validation,
+// launch-shape choice and dispatch to the per-mode launchers. No allocation,
+// no host synchronisation; errors come back as status codes plus a
+// thread-local message.
+#include <atomic>
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <unordered_map>
+
+#include "cutie.h"
+#include "launch.cuh"
+
+namespace cutie {
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char* fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int cuda_fail(cudaError_t e, const char* what) {
+  return fail(CUTIE_ERR_CUDA, "%s: %s (%s)", what, cudaGetErrorString(e), cudaGetErrorName(e));
+}
+
+bool aligned(const void* p, uintptr_t n) { return (reinterpret_cast<uintptr_t>(p) % n) == 0; }
+
+constexpr int kMaxDevices = 64;
+std::atomic<int> g_sm_count[kMaxDevices];
+
+}  // namespace
+
+int device_sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return 0;
+  if (dev >= 0 && dev < kMaxDevices) {
+    const int cached = g_sm_count[dev].load(std::memory_order_relaxed);
+    if (cached > 0) return cached;
+  }
+  int n = 0;
+  if (cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return 0;
+  if (dev >= 0 && dev < kMaxDevices) g_sm_count[dev].store(n, std::memory_order_relaxed);
+  return n;
+}
+
+int cached_blocks_per_sm(const void* kernel, int threads) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, int> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t key = (reinterpret_cast<uint64_t>(kernel) << 16) ^
+                       (static_cast<uint64_t>(threads) << 6) ^ static_cast<uint64_t>(dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  int n = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess)
+    return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = n;
+  return n;
+}
+
+namespace {
+
+int max_threads_for(int nv) { return nv > 4 ? 512 : 1024; }
+
+// Threads per row and vectors per thread for a row of V 16-byte vectors.
+// With few rows, spread each row over more threads (latency); otherwise aim
+// at 4 vectors a thread (enough loads in flight per thread, moderate
+// registers) with the least idle lanes.
+int pick_shape(int64_t V, int64_t M, int requested, LaunchShape* out) {
+  if (requested != 0) {
+    if (requested < 32 || requested > 1024 || requested % 32 != 0)
+      return fail(CUTIE_ERR_INVALID_ARGUMENT,
+                  "threads_per_row must be 0 or a multiple of 32 in [32, 1024], got %d",
+                  requested);
+    int64_t nv = (V + requested - 1) / requested;
+    if (nv < 1) nv = 1;
+    if (nv > 8 || requested > max_threads_for((int)nv))
+      return fail(CUTIE_ERR_UNSUPPORTED,
+                  "threads_per_row=%d leaves %lld vectors per thread for a %lld-vector row "
+                  "(at most 8, and at most 4 above 512 threads)",
+                  requested, (long long)nv, (long long)V);
+    *out = {(int)nv, requested};
+    return CUTIE_OK;
+  }
+  static const int kPrefMany[8] = {4, 3, 5, 2, 6, 7, 8, 1};
+  static const int kPrefFew[8] = {1, 2, 3, 4, 5, 6, 7, 8};
+  const int sms = device_sm_count();
+  const int* pref = (M < 2 * (int64_t)(sms > 0 ? sms : 148)) ? kPrefFew : kPrefMany;
+  int64_t best_waste = -1;
+  for (int i = 0; i < 8; ++i) {
+    const int nv = pref[i];
+    int64_t T = (V + nv - 1) / nv;
+    T = ((T + 31) / 32) * 32;
+    if (T < 32) T = 32;
+    if (T > max_threads_for(nv)) continue;
+    const int64_t waste = T * nv - V;
+    if (best_waste < 0 || waste < best_waste) {
+      best_waste = waste;
+      *out = {nv, (int)T};
+    }
+  }
+  if (best_waste < 0)
+    return fail(CUTIE_ERR_UNSUPPORTED,
+                "row of %lld 16-byte vectors is wider than this build supports (4096)",
+                (long long)V);
+  return CUTIE_OK;
+}
+
+int check_matrix(const char* name, const void* p, int64_t ld, int64_t H, uintptr_t align,
+                 int64_t ld_multiple) {
+  if (p == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "%s is NULL", name);
+  if (ld < H)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "%s: leading dimension %lld < H=%lld", name,
+                (long long)ld, (long long)H);
+  if (!aligned(p, align) || ld % ld_multiple != 0)
+    return fail(CUTIE_ERR_ALIGNMENT,
+                "%s: rows must start %d-byte aligned (pointer %p, leading dimension %lld)",
+                name, (int)align, p, (long long)ld);
+  return CUTIE_OK;
+}
+
+int run_fused(bool norm, const void* x, int64_t ldx, const void* residual, int64_t ldr,
+              const void* weight, float eps, int64_t M, int64_t H, int quant_mode,
+              int group_size, int scale_fmt, int scale_layout, int64_t ld_scale, void* q,
+              int64_t ldq, void* scale, void* residual_out, int64_t ldro, void* normalized_out,
+              int64_t ldn, int threads_per_row, void* stream) {
+  g_err[0] = '\0';
+  if (M < 0 || H <= 0)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "need M >= 0 and H > 0 (got M=%lld, H=%lld)",
+                (long long)M, (long long)H);
+  if (H % 8 != 0)
+    return fail(CUTIE_ERR_UNSUPPORTED, "H=%lld must be a multiple of 8 (16-byte rows)",
+                (long long)H);
+  if (H > (int64_t)1 << 30) return fail(CUTIE_ERR_UNSUPPORTED, "H=%lld too large", (long long)H);
+  if (!(eps >= 0.0f) || std::isinf(eps))
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "eps must be finite and >= 0");
+  if (quant_mode < CUTIE_QUANT_NONE || quant_mode > CUTIE_QUANT_GROUP)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown quant_mode %d", quant_mode);
+  if (scale_fmt < CUTIE_SCALE_FP32 || scale_fmt > CUTIE_SCALE_E8M0)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown scale_fmt %d", scale_fmt);
+  if (scale_layout < CUTIE_LAYOUT_ROW_MAJOR || scale_layout > CUTIE_LAYOUT_MX_SWIZZLED)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown scale_layout %d", scale_layout);
+  const bool quant = quant_mode != CUTIE_QUANT_NONE;
+  if (!norm && !quant)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "quantization-only call without quantization");
+  if (quant_mode == CUTIE_QUANT_GROUP && group_size != 32 && group_size != 64 &&
+      group_size != 128)
+    return fail(CUTIE_ERR_UNSUPPORTED, "group_size must be 32, 64 or 128 (got %d)", group_size);
+  if (residual_out != nullptr && residual == nullptr)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "residual_out requires residual");
+  if (!quant && normalized_out == nullptr && residual_out == nullptr)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "no output requested");
+  if (scale_layout == CUTIE_LAYOUT_MX_SWIZZLED && quant &&
+      (quant_mode != CUTIE_QUANT_GROUP || scale_fmt != CUTIE_SCALE_E8M0))
+    return fail(CUTIE_ERR_INVALID_ARGUMENT,
+                "the swizzled scale layout needs group quantization with E8M0 scales");
+
+  const int64_t n_groups = quant_mode == CUTIE_QUANT_GROUP ? (H + group_size - 1) / group_size : 1;
+  const bool swz = quant && scale_layout == CUTIE_LAYOUT_MX_SWIZZLED;
+  const int64_t n_groups_pad = swz ? (n_groups + 3) / 4 * 4 : n_groups;
+  const int64_t M_pad = swz ? (M + 127) / 128 * 128 : M;
+  if (M_pad == 0) return CUTIE_OK;
+
+  int rc;
+  if ((rc = check_matrix("x", x, ldx, H, 16, 8)) != CUTIE_OK) return rc;
+  if (residual != nullptr && (rc = check_matrix("residual", residual, ldr, H, 16, 8)) != CUTIE_OK)
+    return rc;
+  if (residual_out != nullptr &&
+      (rc = check_matrix("residual_out", residual_out, ldro, H, 16, 8)) != CUTIE_OK)
+    return rc;
+  if (normalized_out != nullptr &&
+      (rc = check_matrix("normalized_out", normalized_out, ldn, H, 16, 8)) != CUTIE_OK)
+    return rc;
+  if (norm) {
+    if (weight == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "weight is NULL");
+    if (!aligned(weight, 16)) return fail(CUTIE_ERR_ALIGNMENT, "weight must be 16-byte aligned");
+  }
+  int64_t s_row = 0, s_grp = 0;
+  if (quant) {
+    if ((rc = check_matrix("q", q, ldq, H, 8, 8)) != CUTIE_OK) return rc;
+    if (scale == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "scale is NULL");
+    if (scale_fmt != CUTIE_SCALE_E8M0 && !aligned(scale, 4))
+      return fail(CUTIE_ERR_ALIGNMENT, "fp32 scales must be 4-byte aligned");
+    if (scale_layout == CUTIE_LAYOUT_ROW_MAJOR) {
+      const int64_t ld = ld_scale == 0 ? n_groups : ld_scale;
+      if (ld < n_groups)
+        return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < %lld groups",
+                    (long long)ld_scale, (long long)n_groups);
+      s_row = ld;
+      s_grp = 1;
+    } else if (scale_layout == CUTIE_LAYOUT_COL_MAJOR) {
+      const int64_t ld = ld_scale == 0 ? M : ld_scale;
+      if (ld < M)
+        return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < M=%lld", (long long)ld_scale,
+                    (long long)M);
+      s_row = 1;
+      s_grp = ld;
+    }
+  }
+
+  const int64_t V = H / 8;
+  LaunchShape sh{};
+  if ((rc = pick_shape(V, M, threads_per_row, &sh)) != CUTIE_OK) return rc;
+
+  FusedArgs a{};
+  a.x = static_cast<const uint16_t*>(x);
+  a.ldx = ldx;
+  a.res = static_cast<const uint16_t*>(residual);
+  a.ldr = ldr;
+  a.w = static_cast<const uint16_t*>(weight);
+  a.res_out = static_cast<uint16_t*>(residual_out);
+  a.ldro = ldro;
+  a.norm_out = static_cast<uint16_t*>(normalized_out);
+  a.ldn = ldn;
+  a.q = static_cast<uint8_t*>(q);
+  a.ldq = ldq;
+  a.scale = scale;
+  a.s_row = s_row;
+  a.s_grp = s_grp;
+  a.M = M;
+  a.M_pad = M_pad;
+  a.H = (int)H;
+  a.V = (int)V;
+  a.n_groups = (int)n_groups;
+  a.n_groups_pad = (int)n_groups_pad;
+  a.eps = eps;
+  a.scale_fmt = scale_fmt;
+  a.scale_layout = swz ? kLaySwizzled : kLayStrided;
+
+  const bool res = residual != nullptr;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e;
+  switch (quant_mode) {
+    case CUTIE_QUANT_NONE: e = launch_fused_none(a, sh, res, norm, st); break;
+    case CUTIE_QUANT_TOKEN: e = launch_fused_token(a, sh, res, norm, st); break;
+    default:
+      e = group_size == 32   ? launch_fused_g32(a, sh, res, norm, st)
+          : group_size == 64 ? launch_fused_g64(a, sh, res, norm, st)
+                             : launch_fused_g128(a, sh, res, norm, st);
+  }
+  if (e != cudaSuccess) return cuda_fail(e, "fused rmsnorm/fp8 launch");
+  return CUTIE_OK;
+}
+
+}  // namespace
+}  // namespace cutie
+
+using namespace cutie;
+
+extern "C" int cutie_rms_norm_fp8(const void* x, int64_t ldx, const void* residual, int64_t ldr,
+                                  const void* weight, float eps, int64_t M, int64_t H,
+                                  int quant_mode, int group_size, int scale_fmt,
+                                  int scale_layout, int64_t ld_scale, void* q, int64_t ldq,
+                                  void* scale, void* residual_out, int64_t ldro,
+                                  void* normalized_out, int64_t ldn, int threads_per_row,
+                                  void* stream) {
+  return run_fused(true, x, ldx, residual, ldr, weight, eps, M, H, quant_mode, group_size,
+                   scale_fmt, scale_layout, ld_scale, q, ldq, scale, residual_out, ldro,
+                   normalized_out, ldn, threads_per_row, stream);
+}
+
+extern "C" int cutie_per_token_cast_to_fp8(const void* x, int64_t ldx, int64_t M, int64_t H,
+                                           int group_size, int scale_fmt, int scale_layout,
+                                           int64_t ld_scale, void* q, int64_t ldq, void* scale,
+                                           int threads_per_row, void* stream) {
+  const int mode = group_size == 0 ? CUTIE_QUANT_TOKEN : CUTIE_QUANT_GROUP;
+  return run_fused(false, x, ldx, nullptr, 0, nullptr, 0.0f, M, H, mode, group_size, scale_fmt,
+                   scale_layout, ld_scale, q, ldq, scale, nullptr, 0, nullptr, 0,
+                   threads_per_row, stream);
+}
+
+extern "C" int cutie_rms_norm(const void* x, int64_t ldx, const void* weight, float eps,
+                              int64_t M, int64_t H, int dtype, void* out, int64_t ldo,
+                              int threads_per_row, void* stream) {
+  if (dtype == CUTIE_DTYPE_BF16) {
+    if (out == nullptr) {
+      g_err[0] = '\0';
+      return fail(CUTIE_ERR_INVALID_ARGUMENT, "out is NULL");
+    }
+    return run_fused(true, x, ldx, nullptr, 0, weight, eps, M, H, CUTIE_QUANT_NONE, 0,
+                     CUTIE_SCALE_FP32, CUTIE_LAYOUT_ROW_MAJOR, 0, nullptr, 0, nullptr, nullptr,
+                     0, out, ldo, threads_per_row, stream);
+  }
+  g_err[0] = '\0';
+  if (dtype != CUTIE_DTYPE_F32) return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown dtype %d", dtype);
+  if (M < 0 || H <= 0)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "need M >= 0 and H > 0 (got M=%lld, H=%lld)",
+                (long long)M, (long long)H);
+  if (H % 4 != 0)
+    return fail(CUTIE_ERR_UNSUPPORTED, "H=%lld must be a multiple of 4 (16-byte rows)",
+                (long long)H);
+  if (H > (int64_t)1 << 30) return fail(CUTIE_ERR_UNSUPPORTED, "H=%lld too large", (long long)H);
+  if (!(eps >= 0.0f) || std::isinf(eps))
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "eps must be finite and >= 0");
+  if (M == 0) return CUTIE_OK;
+  int rc;
+  if ((rc = check_matrix("x", x, ldx, H, 16, 4)) != CUTIE_OK) return rc;
+  if ((rc = check_matrix("out", out, ldo, H, 16, 4)) != CUTIE_OK) return rc;
+  if (weight == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "weight is NULL");
+  if (!aligned(weight, 16)) return fail(CUTIE_ERR_ALIGNMENT, "weight must be 16-byte aligned");
+  LaunchShape sh{};
+  if ((rc = pick_shape(H / 4, M, threads_per_row, &sh)) != CUTIE_OK) return rc;
+  F32Args a{static_cast<const float*>(x), ldx, static_cast<const float*>(weight),
+            static_cast<float*>(out), ldo, M, (int)H, (int)(H / 4), eps};
+  const cudaError_t e = launch_rmsnorm_f32(a, sh, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "fp32 rmsnorm launch");
+  return CUTIE_OK;
+}
+
+extern "C" const char* cutie_last_error(void) { return g_err; }
+
+extern "C" int cutie_abi_version(void) { return CUTIE_ABI_VERSION; }

@@ -1,0 +1,11 @@
+// Instantiations of the fused kernel for one quantization mode (g128).
+#include "launch.cuh"
+
+namespace cutie {
+
+cudaError_t launch_fused_g128(const FusedArgs& a, LaunchShape sh, bool res, bool norm,
+                              cudaStream_t stream) {
+  return launch_fused_mode<kQGroup, 16>(a, sh, res, norm, stream);
+}
+
+}  // namespace cutie

@@ -1,0 +1,211 @@
+"""Tensor-level launchers over the C ABI (include/cutie.h).
+
+These are the destination-passing primitives every public entry point uses:
+the caller passes preallocated CUDA tensors, the work is enqueued on the
+current torch stream of the tensors' device (or on ``stream``), nothing is
+synchronised. Argument errors raise ValueError, CUDA failures CutieError.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .layouts import SCALE_FORMATS, SCALE_LAYOUTS, mx_swizzled_size, n_groups
+
+_FMT_CODE = {"fp32": _lib.SCALE_FP32, "ue8m0": _lib.SCALE_FP32_POW2, "e8m0": _lib.SCALE_E8M0}
+_LAYOUT_CODE = {"row": _lib.LAYOUT_ROW_MAJOR, "col": _lib.LAYOUT_COL_MAJOR, "mx": _lib.LAYOUT_MX_SWIZZLED}
+
+E8M0_DTYPES = tuple(
+    d for d in (getattr(torch, "float8_e8m0fnu", None), torch.uint8) if d is not None
+)
+FP8_DTYPE = torch.float8_e4m3fn
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(device: torch.device, stream) -> int:
+    if stream is None:
+        return torch.cuda.current_stream(device).cuda_stream
+    if isinstance(stream, torch.cuda.Stream):
+        return stream.cuda_stream
+    return int(stream)  # a raw cudaStream_t / CUstream handle
+
+
+def _rows(name: str, t: torch.Tensor, M: int, H: int, dtype: torch.dtype, device) -> int:
+    """Validate a row-major [M, H] matrix view; return its leading dimension."""
+    if not isinstance(t, torch.Tensor):
+        raise TypeError(f"{name} must be a torch.Tensor")
+    if t.dim() != 2 or tuple(t.shape) != (M, H):
+        raise ValueError(f"{name} must have shape ({M}, {H}), got {tuple(t.shape)}")
+    if t.dtype != dtype:
+        raise ValueError(f"{name} must be {dtype}, got {t.dtype}")
+    if t.device != device:
+        raise ValueError(f"{name} is on {t.device}, expected {device}")
+    if H > 1 and t.stride(1) != 1:
+        raise ValueError(f"{name} must be contiguous along its last dimension")
+    return max(t.stride(0), H) if M > 0 else H
+
+
+def _check_x(x: torch.Tensor, dtype=torch.bfloat16) -> tuple[int, int]:
+    if not isinstance(x, torch.Tensor):
+        raise TypeError("x must be a torch.Tensor")
+    if x.dim() != 2:
+        raise ValueError(f"x must be 2-D [M, H], got {x.dim()}-D")
+    if not x.is_cuda:
+        raise ValueError("x must be a CUDA tensor (this library has no CPU path)")
+    if x.dtype != dtype:
+        raise ValueError(f"x must be {dtype}, got {x.dtype}")
+    return x.shape[0], x.shape[1]
+
+
+def _scale_args(scale: torch.Tensor, M: int, H: int, group_size: int | None, fmt: str,
+                layout: str, device) -> int:
+    """Validate the scale tensor for (fmt, layout); return ld_scale."""
+    G = n_groups(H, group_size)
+    if fmt == "e8m0":
+        if scale.dtype not in E8M0_DTYPES:
+            raise ValueError(f"e8m0 scales must be uint8 or float8_e8m0fnu, got {scale.dtype}")
+    elif scale.dtype != torch.float32:
+        raise ValueError(f"{fmt} scales must be float32, got {scale.dtype}")
+    if scale.device != device:
+        raise ValueError(f"scale is on {scale.device}, expected {device}")
+    if layout == "mx":
+        if not scale.is_contiguous() or scale.numel() < mx_swizzled_size(M, G):
+            raise ValueError(
+                f"swizzled scales need a contiguous buffer of {mx_swizzled_size(M, G)} bytes"
+            )
+        return 0
+    if scale.dim() == 1 and G == 1:
+        if scale.shape[0] != M or (M > 1 and scale.stride(0) != 1):
+            raise ValueError(f"per-token scale must be a contiguous [{M}] tensor")
+        return M if layout == "col" else 1
+    if scale.dim() != 2:
+        raise ValueError("scale must be 2-D")
+    shape = tuple(scale.shape)
+    if layout == "row":
+        if shape != (M, G):
+            raise ValueError(f"row-major scale must have shape ({M}, {G}), got {shape}")
+        if G > 1 and scale.stride(1) != 1:
+            raise ValueError("row-major scale must be contiguous along groups")
+        return max(scale.stride(0), G) if M > 1 else G
+    # column-major: a [G, M] tensor, or its transposed [M, G] view
+    if shape == (G, M) and (M <= 1 or scale.stride(1) == 1):
+        return max(scale.stride(0), M) if G > 1 else M
+    if shape == (M, G) and (M <= 1 or scale.stride(0) == 1):
+        return max(scale.stride(1), M) if G > 1 else M
+    raise ValueError(
+        f"column-major scale must be a [{G}, {M}] tensor contiguous along M (or its transpose)"
+    )
+
+
+def launch_rms_norm_fp8(
+    x: torch.Tensor,
+    weight: torch.Tensor | None,
+    eps: float,
+    *,
+    residual: torch.Tensor | None = None,
+    q: torch.Tensor | None = None,
+    scale: torch.Tensor | None = None,
+    residual_out: torch.Tensor | None = None,
+    normalized_out: torch.Tensor | None = None,
+    group_size: int | None = 128,
+    scale_format: str = "fp32",
+    scale_layout: str = "row",
+    threads_per_row: int = 0,
+    normalize: bool = True,
+    stream=None,
+) -> None:
+    """Enqueue one fused [residual add] -> RMSNorm -> [FP8 quant] launch.
+
+    ``q`` and ``scale`` both None means no quantization. ``group_size`` None
+    (or 0) means one scale per row. ``normalize=False`` quantizes ``x`` as is.
+    """
+    M, H = _check_x(x)
+    device = x.device
+    if scale_format not in SCALE_FORMATS:
+        raise ValueError(f"scale_format must be one of {SCALE_FORMATS}")
+    if scale_layout not in SCALE_LAYOUTS:
+        raise ValueError(f"scale_layout must be one of {SCALE_LAYOUTS}")
+    ldx = _rows("x", x, M, H, torch.bfloat16, device)
+    ldr = _rows("residual", residual, M, H, torch.bfloat16, device) if residual is not None else 0
+    ldro = (
+        _rows("residual_out", residual_out, M, H, torch.bfloat16, device)
+        if residual_out is not None
+        else 0
+    )
+    ldn = (
+        _rows("normalized_out", normalized_out, M, H, torch.bfloat16, device)
+        if normalized_out is not None
+        else 0
+    )
+    if normalize:
+        if weight is None:
+            raise ValueError("weight is required")
+        if weight.shape != (H,) or weight.dtype != torch.bfloat16 or weight.device != device:
+            raise ValueError(f"weight must be a bf16 [{H}] tensor on {device}")
+        if not weight.is_contiguous():
+            raise ValueError("weight must be contiguous")
+    quant = q is not None or scale is not None
+    if quant:
+        if q is None or scale is None:
+            raise ValueError("q and scale must be given together")
+        if q.dtype not in (FP8_DTYPE, torch.uint8):
+            raise ValueError(f"q must be float8_e4m3fn, got {q.dtype}")
+        ldq = _rows("q", q, M, H, q.dtype, device)
+        ld_scale = _scale_args(scale, M, H, group_size, scale_format, scale_layout, device)
+        mode = _lib.QUANT_GROUP if group_size else _lib.QUANT_TOKEN
+    else:
+        ldq, ld_scale, mode = 0, 0, _lib.QUANT_NONE
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        handle = _stream_handle(device, stream)
+        if normalize:
+            status = lib.cutie_rms_norm_fp8(
+                _ptr(x), ldx, _ptr(residual), ldr, _ptr(weight), float(eps), M, H,
+                mode, int(group_size or 0), _FMT_CODE[scale_format],
+                _LAYOUT_CODE[scale_layout], ld_scale, _ptr(q), ldq, _ptr(scale),
+                _ptr(residual_out), ldro, _ptr(normalized_out), ldn,
+                int(threads_per_row), handle,
+            )
+        else:
+            if not quant:
+                raise ValueError("quantization-only call needs q and scale")
+            status = lib.cutie_per_token_cast_to_fp8(
+                _ptr(x), ldx, M, H, int(group_size or 0), _FMT_CODE[scale_format],
+                _LAYOUT_CODE[scale_layout], ld_scale, _ptr(q), ldq, _ptr(scale),
+                int(threads_per_row), handle,
+            )
+    _lib.check(status)
+
+
+def launch_rms_norm(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float,
+    out: torch.Tensor,
+    *,
+    threads_per_row: int = 0,
+    stream=None,
+) -> None:
+    """Enqueue a standalone RMSNorm (bf16 or fp32, see include/cutie.h)."""
+    if x.dtype not in (torch.bfloat16, torch.float32):
+        raise ValueError(f"x must be bfloat16 or float32, got {x.dtype}")
+    M, H = _check_x(x, x.dtype)
+    device = x.device
+    ldx = _rows("x", x, M, H, x.dtype, device)
+    ldo = _rows("out", out, M, H, x.dtype, device)
+    if weight.shape != (H,) or weight.dtype != x.dtype or weight.device != device:
+        raise ValueError(f"weight must be a {x.dtype} [{H}] tensor on {device}")
+    if not weight.is_contiguous():
+        raise ValueError("weight must be contiguous")
+    code = _lib.DTYPE_BF16 if x.dtype == torch.bfloat16 else _lib.DTYPE_F32
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        status = lib.cutie_rms_norm(
+            _ptr(x), ldx, _ptr(weight), float(eps), M, H, code, _ptr(out), ldo,
+            int(threads_per_row), _stream_handle(device, stream),
+        )
+    _lib.check(status)
