@@ -55,6 +55,8 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=0, help="0: min(steps, 20)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-clocks", action="store_true",
+                    help="skip clock sampling and its soak (profiling runs)")
     ap.add_argument("--cpu-seconds", type=float, default=12.0,
                     help="target CPU work for the cpu_baseline sample")
     args = ap.parse_args()
@@ -233,21 +235,23 @@ def run_ours(args, rank, world, local_rank):
     K = args.steps
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(K)]
-    clocks = ClockSampler(local_rank)
+    clocks = ClockSampler(local_rank) if not args.no_clocks else None
     barrier()
     torch.cuda.synchronize(device)
-    clocks.start()
+    if clocks:
+        clocks.start()
     for i in range(K):
         starts[i].record(stream)
         step(i)
         ends[i].record(stream)
     torch.cuda.synchronize(device)
-    clocks.stop()
+    if clocks:
+        clocks.stop()
     barrier()
     total_ms = starts[0].elapsed_time(ends[-1])
     launch_ms = statistics.fmean(s.elapsed_time(e) for s, e in zip(starts, ends))
     window = "timed"
-    if len(clocks.samples) < 5:
+    if clocks and len(clocks.samples) < 5:
         # The timed region was too short for the sampler: keep the same launches
         # running for ~1 s more (untimed) so the clock record covers the load.
         t_end = time.monotonic() + 1.0
@@ -367,7 +371,7 @@ def run_ours(args, rank, world, local_rank):
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": K,
-        "clocks": clocks.summary(window),
+        "clocks": clocks.summary(window) if clocks else None,
     }
     if rank == 0:
         print(json.dumps(result), flush=True)

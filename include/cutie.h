@@ -145,6 +145,16 @@ CUTIE_API int cutie_rms_norm(const void* x, int64_t ldx, const void* weight, flo
                    int64_t M, int64_t H, int dtype,
                    void* out, int64_t ldo, int threads_per_row, void* stream);
 
+/*
+ * Device-side status of this library's kernels on the current device: 0 when
+ * no kernel has hit a failure since the last clear; otherwise the first error
+ * code recorded (1 = a bulk-copy wait ran out: a row never arrived in shared
+ * memory within ~2 s and the kernel stopped early, leaving outputs
+ * incomplete). Synchronises with the device; `clear` != 0 resets the word.
+ * A negative return is a CUDA failure (see cutie_last_error()).
+ */
+CUTIE_API int cutie_device_error(int clear);
+
 /* Message of the last failing call on this thread ("" if none). */
 CUTIE_API const char* cutie_last_error(void);
 

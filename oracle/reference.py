@@ -45,10 +45,22 @@ def rms_norm_reference(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-6)
     return normalized.to(x.dtype) * weight
 
 
-def rms_norm_f32(x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:
-    """rms_norm.py:11-20 — the standalone fp32 RMSNorm, evaluated eagerly."""
+def rms_norm_f32(
+    x: torch.Tensor, weight: torch.Tensor, eps: float = 1e-5, ieee_sqrt: bool = True
+) -> torch.Tensor:
+    """rms_norm.py:11-20 — the standalone fp32 RMSNorm.
+
+    The reference runs this under torch.compile on the GPU, where the square
+    root is the IEEE (correctly rounded) one. Eager torch on the CPU is not
+    always: on AVX-512 builds its float32 sqrt was observed 1 ulp off
+    (sqrt(1.360060215) -> 1.1662161 instead of 1.1662163). ieee_sqrt=True
+    (default) takes the square root in float64 and rounds it to float32,
+    which is the correctly rounded float32 square root (the double rounding
+    is innocuous for sqrt); ieee_sqrt=False is the literal eager expression.
+    """
     variance = x.pow(2).mean(dim=-1, keepdim=True) + eps
-    x = x / torch.sqrt(variance)
+    root = torch.sqrt(variance.double()).float() if ieee_sqrt else torch.sqrt(variance)
+    x = x / root
     return x * weight
 
 

@@ -70,8 +70,10 @@ def check_parity(inp: dict, group_size, fmt: str, layout: str, *, exact: bool = 
                  threads: int = 0, budget: float = 1e-3) -> dict:
     """Run GPU and oracle on the same inputs; assert the tolerance contract.
 
-    residual_out: bit-exact. normalized: at most 1 bf16 ulp on <= budget of
-    elements (fp32 sum order is the only difference). Quantization of the
+    residual_out: bit-exact. normalized: at most 2 bf16 ulps on <= budget of
+    elements (fp32 sum order is the only difference: inv_rms moves by an fp32
+    ulp, bf16(r * inv) by at most one bf16 ulp, and the bf16 weight product can
+    turn that into two when it drops into the binade below). Quantization of the
     GPU's own normalized output: bit-exact (scales and codes). End to end:
     scales bit-exact wherever the group's normalized values agree, codes within
     1 e4m3 ulp on <= budget of elements. exact=True: everything bit-exact.
@@ -90,7 +92,7 @@ def check_parity(inp: dict, group_size, fmt: str, layout: str, *, exact: bool = 
     if exact:
         assert nd.max(initial=0) == 0, "normalized differs on exact-sum inputs"
     else:
-        assert nd.max(initial=0) <= 1
+        assert nd.max(initial=0) <= 2
         assert stats["normalized_diff_frac"] <= budget
     # quantization stage, fed the GPU's own normalized values: bit-exact
     qc = q_codes(q)
@@ -117,7 +119,7 @@ def check_parity(inp: dict, group_size, fmt: str, layout: str, *, exact: bool = 
     else:
         if fmt == "fp32" and (~group_same).any():
             rel = np.abs(sm[~group_same] - sr[~group_same]) / sr[~group_same]
-            assert rel.max() <= 2.0**-7, "scale moved by more than one bf16 ulp of amax"
+            assert rel.max() <= 2.0**-6, "scale moved by more than two bf16 ulps of amax"
         assert qd.max(initial=0) <= 1
         assert stats["q_diff_frac"] <= budget
     return stats

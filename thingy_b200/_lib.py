@@ -32,6 +32,7 @@ EXPORTED_SYMBOLS = (
     "cutie_rms_norm_fp8",
     "cutie_per_token_cast_to_fp8",
     "cutie_rms_norm",
+    "cutie_device_error",
     "cutie_last_error",
     "cutie_abi_version",
 )
@@ -55,6 +56,7 @@ _SIGNATURES = {
         _int,
         [_ptr, _i64, _ptr, _f32, _i64, _i64, _int, _ptr, _i64, _int, _ptr],
     ),
+    "cutie_device_error": (_int, [_int]),
     "cutie_last_error": (ctypes.c_char_p, []),
     "cutie_abi_version": (_int, []),
 }
@@ -94,6 +96,14 @@ def load() -> ctypes.CDLL:
             raise RuntimeError(f"{_LIB_PATH} has ABI version {version}, expected {ABI_VERSION}")
         _lib = lib
         return lib
+
+
+def device_error(clear: bool = True) -> int:
+    """The library's device-side error word on the current device (0 = none)."""
+    status = load().cutie_device_error(1 if clear else 0)
+    if status < 0:
+        check(status)
+    return status
 
 
 def check(status: int) -> None:

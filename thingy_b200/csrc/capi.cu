@@ -50,20 +50,21 @@ int device_sm_count() {
   return n;
 }
 
-int cached_blocks_per_sm(const void* kernel, int threads) {
+int cached_blocks_per_sm(const void* kernel, int threads, int dyn_smem) {
   static std::mutex mu;
   static std::unordered_map<uint64_t, int> cache;
   int dev = 0;
   cudaGetDevice(&dev);
-  const uint64_t key = (reinterpret_cast<uint64_t>(kernel) << 16) ^
-                       (static_cast<uint64_t>(threads) << 6) ^ static_cast<uint64_t>(dev);
+  const uint64_t key = (reinterpret_cast<uint64_t>(kernel) * 0x9E3779B97F4A7C15ull) ^
+                       (static_cast<uint64_t>(threads) << 40) ^
+                       (static_cast<uint64_t>(dyn_smem) << 8) ^ static_cast<uint64_t>(dev);
   {
     std::lock_guard<std::mutex> lock(mu);
     auto it = cache.find(key);
     if (it != cache.end()) return it->second;
   }
   int n = 0;
-  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, 0) != cudaSuccess)
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, kernel, threads, dyn_smem) != cudaSuccess)
     return 0;
   std::lock_guard<std::mutex> lock(mu);
   cache[key] = n;
@@ -71,14 +72,139 @@ int cached_blocks_per_sm(const void* kernel, int threads) {
 }
 
 namespace {
+std::mutex g_attr_mu;
+std::unordered_map<const void*, int> g_attr_raised;  // kernel -> dynamic smem limit set
+}  // namespace
 
-int max_threads_for(int nv) { return nv > 4 ? 512 : 1024; }
+int set_smem_and_occupancy(const void* kernel, int threads, int smem) {
+  {
+    std::lock_guard<std::mutex> lock(g_attr_mu);
+    int& have = g_attr_raised[kernel];
+    if (smem > have) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) !=
+          cudaSuccess)
+        return 0;
+      have = smem;
+    }
+  }
+  return cached_blocks_per_sm(kernel, threads, smem);
+}
 
-// Threads per row and vectors per thread for a row of V 16-byte vectors.
-// With few rows, spread each row over more threads (latency); otherwise aim
-// at 4 vectors a thread (enough loads in flight per thread, moderate
-// registers) with the least idle lanes.
-int pick_shape(int64_t V, int64_t M, int requested, LaunchShape* out) {
+// Ring depth of the warp-per-row kernel (2 KB slots per warp).
+int rowwarp_stages() { return 3; }
+
+BulkPlan plan_bulk(const void* kernel, int threads, int stage_bytes, int max_stages) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, BulkPlan> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t key = (reinterpret_cast<uint64_t>(kernel) * 0x9E3779B97F4A7C15ull) ^
+                       (static_cast<uint64_t>(threads) << 44) ^
+                       (static_cast<uint64_t>(stage_bytes) << 12) ^
+                       (static_cast<uint64_t>(max_stages) << 6) ^ static_cast<uint64_t>(dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  BulkPlan plan{0, 0, 0};
+  int sm_smem = 0, block_smem = 0, reserved = 0;
+  cudaFuncAttributes attr{};
+  if (cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) !=
+          cudaSuccess ||
+      cudaDeviceGetAttribute(&block_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+          cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) !=
+          cudaSuccess ||
+      cudaFuncGetAttributes(&attr, kernel) != cudaSuccess)
+    return plan;
+  const int by_regs = cached_blocks_per_sm(kernel, threads, 0);
+  // Prefer >= 2 stages (prefetch two rows ahead); rows too wide for that on
+  // one SM still run with one stage (its refill overlaps the row's compute).
+  for (int b = by_regs; b >= 1 && plan.stages < 2; --b) {
+    int room = sm_smem / b - reserved - (int)attr.sharedSizeBytes;
+    if (room > block_smem - (int)attr.sharedSizeBytes) room = block_smem - (int)attr.sharedSizeBytes;
+    int stages = room / (stage_bytes + 8);
+    if (stages > max_stages) stages = max_stages;
+    if (stages >= 2) {
+      plan.stages = stages;
+      plan.blocks_per_sm = b;
+      plan.smem_bytes = stages * (stage_bytes + 8);
+    }
+  }
+  if (plan.stages < 2) {
+    int room = block_smem - (int)attr.sharedSizeBytes - reserved;
+    if (room >= stage_bytes + 8) plan = BulkPlan{1, 1, stage_bytes + 8};
+  }
+  if (plan.stages >= 1) {
+    // The limit is a property of the kernel, shared by every plan of it:
+    // it is only ever raised, so plans cached for larger rows stay launchable.
+    const int n = set_smem_and_occupancy(kernel, threads, plan.smem_bytes);
+    if (n <= 0) plan = BulkPlan{0, 0, 0};
+    else plan.blocks_per_sm = n;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = plan;
+  return plan;
+}
+
+namespace {
+
+
+// Launch shape for a row of V 16-byte vectors (NC 64-byte chunks).
+//  * threads_per_row == 32: one warp per row, the two-pass kernel (any H).
+//  * larger requests, and the automatic choice: the single-pass kernel with
+//    one CTA per row, one chunk per thread (two when the row is wider than
+//    1024 chunks); rows wider than that stream through the warp-per-row
+//    kernel (unless an output aliases an input: it re-reads its inputs).
+int pick_shape(int64_t V, int64_t M, int requested, bool aliased, LaunchShape* out) {
+  const int64_t NC = (V + 3) / 4;
+  if (requested == 32) {
+    if (aliased)
+      return fail(CUTIE_ERR_UNSUPPORTED,
+                  "threads_per_row=32 (one warp per row) re-reads its inputs and cannot run "
+                  "with an output that aliases an input");
+    *out = {1, 32, true};
+    return CUTIE_OK;
+  }
+  if (requested != 0) {
+    if (requested < 32 || requested > 1024 || requested % 32 != 0)
+      return fail(CUTIE_ERR_INVALID_ARGUMENT,
+                  "threads_per_row must be 0 or a multiple of 32 in [32, 1024], got %d",
+                  requested);
+    const int64_t nch = (NC + requested - 1) / requested;
+    if (nch > 2 || (nch == 2 && requested > 512))
+      return fail(CUTIE_ERR_UNSUPPORTED,
+                  "threads_per_row=%d leaves %lld 64-byte chunks per thread for a %lld-chunk "
+                  "row (at most 1, or 2 with at most 512 threads)",
+                  requested, (long long)nch, (long long)NC);
+    *out = {nch < 1 ? 1 : (int)nch, requested, false};
+    return CUTIE_OK;
+  }
+  int64_t T = (NC + 31) / 32 * 32;
+  if (T < 32) T = 32;
+  if (T <= 1024) {
+    *out = {1, (int)T, false};
+    return CUTIE_OK;
+  }
+  T = ((NC + 1) / 2 + 31) / 32 * 32;
+  if (T <= 512) {
+    *out = {2, (int)T, false};
+    return CUTIE_OK;
+  }
+  if (!aliased) {  // wider rows than one CTA can hold: stream them per warp
+    *out = {1, 32, true};
+    return CUTIE_OK;
+  }
+  return fail(CUTIE_ERR_UNSUPPORTED,
+              "H=%lld with an output aliasing an input is wider than the single-pass kernel "
+              "supports (32768)",
+              (long long)V * 8);
+}
+
+// fp32 kernel: NV 16-byte vectors (4 floats) a thread, least idle lanes.
+int pick_f32_shape(int64_t V, int64_t M, int requested, F32Shape* out) {
+  auto max_threads_for = [](int nv) { return nv > 4 ? 512 : 1024; };
   if (requested != 0) {
     if (requested < 32 || requested > 1024 || requested % 32 != 0)
       return fail(CUTIE_ERR_INVALID_ARGUMENT,
@@ -88,8 +214,7 @@ int pick_shape(int64_t V, int64_t M, int requested, LaunchShape* out) {
     if (nv < 1) nv = 1;
     if (nv > 8 || requested > max_threads_for((int)nv))
       return fail(CUTIE_ERR_UNSUPPORTED,
-                  "threads_per_row=%d leaves %lld vectors per thread for a %lld-vector row "
-                  "(at most 8, and at most 4 above 512 threads)",
+                  "threads_per_row=%d leaves %lld vectors per thread for a %lld-vector row",
                   requested, (long long)nv, (long long)V);
     *out = {(int)nv, requested};
     return CUTIE_OK;
@@ -112,9 +237,8 @@ int pick_shape(int64_t V, int64_t M, int requested, LaunchShape* out) {
     }
   }
   if (best_waste < 0)
-    return fail(CUTIE_ERR_UNSUPPORTED,
-                "row of %lld 16-byte vectors is wider than this build supports (4096)",
-                (long long)V);
+    return fail(CUTIE_ERR_UNSUPPORTED, "H=%lld is wider than this build supports (16384)",
+                (long long)V * 4);
   return CUTIE_OK;
 }
 
@@ -212,7 +336,10 @@ int run_fused(bool norm, const void* x, int64_t ldx, const void* residual, int64
 
   const int64_t V = H / 8;
   LaunchShape sh{};
-  if ((rc = pick_shape(V, M, threads_per_row, &sh)) != CUTIE_OK) return rc;
+  const bool aliased =
+      (residual_out != nullptr && (residual_out == x || residual_out == residual)) ||
+      (normalized_out != nullptr && (normalized_out == x || normalized_out == residual));
+  if ((rc = pick_shape(V, M, threads_per_row, aliased, &sh)) != CUTIE_OK) return rc;
 
   FusedArgs a{};
   a.x = static_cast<const uint16_t*>(x);
@@ -236,8 +363,10 @@ int run_fused(bool norm, const void* x, int64_t ldx, const void* residual, int64
   a.n_groups = (int)n_groups;
   a.n_groups_pad = (int)n_groups_pad;
   a.eps = eps;
+  a.rcp_H = 1.0f / (float)H;
   a.scale_fmt = scale_fmt;
   a.scale_layout = swz ? kLaySwizzled : kLayStrided;
+  a.stages = 0;
 
   const bool res = residual != nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -310,13 +439,27 @@ extern "C" int cutie_rms_norm(const void* x, int64_t ldx, const void* weight, fl
   if ((rc = check_matrix("out", out, ldo, H, 16, 4)) != CUTIE_OK) return rc;
   if (weight == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "weight is NULL");
   if (!aligned(weight, 16)) return fail(CUTIE_ERR_ALIGNMENT, "weight must be 16-byte aligned");
-  LaunchShape sh{};
-  if ((rc = pick_shape(H / 4, M, threads_per_row, &sh)) != CUTIE_OK) return rc;
+  F32Shape sh{};
+  if ((rc = pick_f32_shape(H / 4, M, threads_per_row, &sh)) != CUTIE_OK) return rc;
   F32Args a{static_cast<const float*>(x), ldx, static_cast<const float*>(weight),
             static_cast<float*>(out), ldo, M, (int)H, (int)(H / 4), eps};
   const cudaError_t e = launch_rmsnorm_f32(a, sh, static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "fp32 rmsnorm launch");
   return CUTIE_OK;
+}
+
+extern "C" int cutie_device_error(int clear) {
+  g_err[0] = '\0';
+  int any = 0;
+  cudaError_t (*readers[])(int*, bool) = {device_error_none, device_error_token, device_error_g32,
+                                          device_error_g64, device_error_g128};
+  for (auto read : readers) {
+    int v = 0;
+    const cudaError_t e = read(&v, clear != 0);
+    if (e != cudaSuccess) return cuda_fail(e, "reading the device error word");
+    if (any == 0) any = v;
+  }
+  return any;
 }
 
 extern "C" const char* cutie_last_error(void) { return g_err; }

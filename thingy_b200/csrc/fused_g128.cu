@@ -1,11 +1,13 @@
-// Instantiations of the fused kernel for one quantization mode (g128).
+// Instantiations of the fused kernels for one quantization mode (g128).
 #include "launch.cuh"
 
 namespace cutie {
 
 cudaError_t launch_fused_g128(const FusedArgs& a, LaunchShape sh, bool res, bool norm,
                               cudaStream_t stream) {
-  return launch_fused_mode<kQGroup, 16>(a, sh, res, norm, stream);
+  return launch_fused_mode<kQGroup, 4>(a, sh, res, norm, stream);
 }
+
+cudaError_t device_error_g128(int* out, bool clear) { return read_device_error(out, clear); }
 
 }  // namespace cutie

@@ -7,60 +7,118 @@
 
 namespace cutie {
 
-// Defined in capi.cu. Both are cached per device / per (kernel, block size).
+// Defined in capi.cu; cached per device / per (kernel, block size, bytes).
 int device_sm_count();
-int cached_blocks_per_sm(const void* kernel, int threads);
+int cached_blocks_per_sm(const void* kernel, int threads, int dyn_smem);
 
-// Persistent grid: as many CTAs as can be resident at once, never more than
-// the number of rows to walk.
-template <int NV, int QM, int GL, bool RES, bool NORM>
-cudaError_t launch_fused_one(const FusedArgs& a, int threads, cudaStream_t stream) {
-  auto kernel = fused_rmsnorm_fp8_kernel<NV, QM, GL, RES, NORM>;
-  const int per_sm = cached_blocks_per_sm(reinterpret_cast<const void*>(kernel), threads);
-  if (per_sm <= 0) return cudaErrorInvalidConfiguration;
-  int64_t grid = (int64_t)per_sm * device_sm_count();
+// Ring plan: the most CTAs per SM (up to what registers allow) that still
+// leave room for >= 2 stages each, and up to `max_stages` stages. Raises the
+// kernel's dynamic shared-memory limit when needed. stages < 2: no plan.
+struct BulkPlan {
+  int stages;
+  int blocks_per_sm;
+  int smem_bytes;
+};
+BulkPlan plan_bulk(const void* kernel, int threads, int stage_bytes, int max_stages);
+
+// Raise the kernel's dynamic shared-memory limit to `smem` (never lowers it)
+// and return the resident CTAs per SM at that size (0 on failure).
+int set_smem_and_occupancy(const void* kernel, int threads, int smem);
+
+constexpr int kMaxStages = 4;
+
+// Persistent grid: as many CTAs as can be resident, never more than rows.
+template <int NCH, int QM, int LPG, bool RES, bool NORM, bool FULL>
+cudaError_t launch_fused_one(FusedArgs a, int threads, cudaStream_t stream) {
+  auto kernel = fused_rmsnorm_fp8_kernel<NCH, QM, LPG, RES, NORM, FULL>;
+  const int row_pad = (a.V * 16 + 63) / 64 * 64 + 64;  // whole chunks + one zero chunk
+  const int stage_bytes = row_pad * (RES ? 2 : 1);
+  const BulkPlan p =
+      plan_bulk(reinterpret_cast<const void*>(kernel), threads, stage_bytes, kMaxStages);
+  if (p.stages < 1) return cudaErrorInvalidConfiguration;
+  a.stages = p.stages;
+  int64_t grid = (int64_t)p.blocks_per_sm * device_sm_count();
   if (grid > a.M_pad) grid = a.M_pad;
   if (grid <= 0) return cudaSuccess;
-  kernel<<<(unsigned)grid, threads, 0, stream>>>(a);
+  kernel<<<(unsigned)grid, threads, p.smem_bytes, stream>>>(a);
   return cudaGetLastError();
 }
 
-template <int QM, int GL, bool RES, bool NORM>
-cudaError_t launch_fused_nv(const FusedArgs& a, LaunchShape sh, cudaStream_t stream) {
-  switch (sh.nv) {
-    case 1: return launch_fused_one<1, QM, GL, RES, NORM>(a, sh.threads, stream);
-    case 2: return launch_fused_one<2, QM, GL, RES, NORM>(a, sh.threads, stream);
-    case 3: return launch_fused_one<3, QM, GL, RES, NORM>(a, sh.threads, stream);
-    case 4: return launch_fused_one<4, QM, GL, RES, NORM>(a, sh.threads, stream);
-    case 5: return launch_fused_one<5, QM, GL, RES, NORM>(a, sh.threads, stream);
-    case 6: return launch_fused_one<6, QM, GL, RES, NORM>(a, sh.threads, stream);
-    case 7: return launch_fused_one<7, QM, GL, RES, NORM>(a, sh.threads, stream);
-    case 8: return launch_fused_one<8, QM, GL, RES, NORM>(a, sh.threads, stream);
+// Warp-per-row kernel: kRowwarpWarps warps per CTA, a private ring of
+// `stages` 2 KB piece slots per warp; persistent grid over rows.
+int rowwarp_stages();
+template <int QM, int LPG, bool RES, bool NORM, bool FULL>
+cudaError_t launch_rowwarp_one(FusedArgs a, cudaStream_t stream) {
+  auto kernel = rowwarp_rmsnorm_fp8_kernel<QM, LPG, RES, NORM, FULL>;
+  constexpr int kThreads = kRowwarpWarps * 32;
+  const int P = rowwarp_stages();
+  const int slot = (int)kPieceBytes * (RES ? 2 : 1);
+  const int smem = kRowwarpWarps * P * (slot + 8);
+  const int per_sm = set_smem_and_occupancy(reinterpret_cast<const void*>(kernel), kThreads, smem);
+  if (per_sm <= 0) return cudaErrorInvalidConfiguration;
+  a.stages = P;
+  int64_t grid = (int64_t)per_sm * device_sm_count();
+  const int64_t need = (a.M_pad + kRowwarpWarps - 1) / kRowwarpWarps;
+  if (grid > need) grid = need;
+  if (grid <= 0) return cudaSuccess;
+  kernel<<<(unsigned)grid, kThreads, smem, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <int QM, int LPG, bool RES, bool NORM>
+cudaError_t launch_fused_nch(const FusedArgs& a, LaunchShape sh, cudaStream_t stream) {
+  if (sh.rowwarp) {
+    // no bounds predicates when the row is whole 2 KB pieces
+    const bool full = a.V % 128 == 0;
+    return full ? launch_rowwarp_one<QM, LPG, RES, NORM, true>(a, stream)
+                : launch_rowwarp_one<QM, LPG, RES, NORM, false>(a, stream);
+  }
+  // Rows that fill every thread's chunks exactly take the kernel without
+  // store predicates.
+  const bool full = (int64_t)sh.threads * sh.nch * 4 == a.V;
+  switch (sh.nch * 2 + (full ? 1 : 0)) {
+    case 2: return launch_fused_one<1, QM, LPG, RES, NORM, false>(a, sh.threads, stream);
+    case 3: return launch_fused_one<1, QM, LPG, RES, NORM, true>(a, sh.threads, stream);
+    case 4: return launch_fused_one<2, QM, LPG, RES, NORM, false>(a, sh.threads, stream);
+    case 5: return launch_fused_one<2, QM, LPG, RES, NORM, true>(a, sh.threads, stream);
     default: return cudaErrorInvalidValue;
   }
 }
 
-template <int QM, int GL>
+template <int QM, int LPG>
 cudaError_t launch_fused_mode(const FusedArgs& a, LaunchShape sh, bool res, bool norm,
                               cudaStream_t stream) {
   if (!norm) {
-    if constexpr (QM != kQNone) return launch_fused_nv<QM, GL, false, false>(a, sh, stream);
+    if constexpr (QM != kQNone) return launch_fused_nch<QM, LPG, false, false>(a, sh, stream);
     return cudaErrorInvalidValue;
   }
-  return res ? launch_fused_nv<QM, GL, true, true>(a, sh, stream)
-             : launch_fused_nv<QM, GL, false, true>(a, sh, stream);
+  return res ? launch_fused_nch<QM, LPG, true, true>(a, sh, stream)
+             : launch_fused_nch<QM, LPG, false, true>(a, sh, stream);
 }
 
-cudaError_t launch_fused_none(const FusedArgs& a, LaunchShape sh, bool res, bool norm,
-                              cudaStream_t stream);
-cudaError_t launch_fused_token(const FusedArgs& a, LaunchShape sh, bool res, bool norm,
-                               cudaStream_t stream);
-cudaError_t launch_fused_g32(const FusedArgs& a, LaunchShape sh, bool res, bool norm,
-                             cudaStream_t stream);
-cudaError_t launch_fused_g64(const FusedArgs& a, LaunchShape sh, bool res, bool norm,
-                             cudaStream_t stream);
-cudaError_t launch_fused_g128(const FusedArgs& a, LaunchShape sh, bool res, bool norm,
-                              cudaStream_t stream);
+// Read (and optionally clear) this translation unit's device error word.
+inline cudaError_t read_device_error(int* out, bool clear) {
+  int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_cutie_device_error, sizeof(int));
+  if (e != cudaSuccess) return e;
+  if (clear && v != 0) {
+    const int zero = 0;
+    e = cudaMemcpyToSymbol(g_cutie_device_error, &zero, sizeof(int));
+  }
+  *out = v;
+  return e;
+}
+
+#define CUTIE_DECLARE_MODE(name)                                                          \
+  cudaError_t launch_fused_##name(const FusedArgs& a, LaunchShape sh, bool res, bool norm, \
+                                  cudaStream_t stream);                                   \
+  cudaError_t device_error_##name(int* out, bool clear);
+
+CUTIE_DECLARE_MODE(none)
+CUTIE_DECLARE_MODE(token)
+CUTIE_DECLARE_MODE(g32)
+CUTIE_DECLARE_MODE(g64)
+CUTIE_DECLARE_MODE(g128)
 
 struct F32Args {
   const float* x;
@@ -74,6 +132,11 @@ struct F32Args {
   float eps;
 };
 
-cudaError_t launch_rmsnorm_f32(const F32Args& a, LaunchShape sh, cudaStream_t stream);
+// The fp32 kernel keeps its own register layout (NV vectors a thread).
+struct F32Shape {
+  int nv;
+  int threads;
+};
+cudaError_t launch_rmsnorm_f32(const F32Args& a, F32Shape sh, cudaStream_t stream);
 
 }  // namespace cutie

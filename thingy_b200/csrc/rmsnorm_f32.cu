@@ -67,8 +67,9 @@ __global__ void __launch_bounds__(NV > 4 ? 512 : 1024) rmsnorm_f32_kernel(const 
       if (fabsf(hi.y) < 0x1p-100f) hi.y = __fdiv_rn(v[k].w, sd);
       lo = __fmul2_rn(lo, make_float2(w[k].x, w[k].y));
       hi = __fmul2_rn(hi, make_float2(w[k].z, w[k].w));
-      st_stream(orow + (int64_t)vi * 4, __float_as_uint(lo.x), __float_as_uint(lo.y),
-                __float_as_uint(hi.x), __float_as_uint(hi.y));
+      const uint32_t out4[4] = {__float_as_uint(lo.x), __float_as_uint(lo.y),
+                                __float_as_uint(hi.x), __float_as_uint(hi.y)};
+      st_stream(orow + (int64_t)vi * 4, out4);
     }
   }
 }
@@ -76,7 +77,7 @@ __global__ void __launch_bounds__(NV > 4 ? 512 : 1024) rmsnorm_f32_kernel(const 
 template <int NV>
 static cudaError_t launch_f32_one(const F32Args& a, int threads, cudaStream_t stream) {
   auto kernel = rmsnorm_f32_kernel<NV>;
-  const int per_sm = cached_blocks_per_sm(reinterpret_cast<const void*>(kernel), threads);
+  const int per_sm = cached_blocks_per_sm(reinterpret_cast<const void*>(kernel), threads, 0);
   if (per_sm <= 0) return cudaErrorInvalidConfiguration;
   int64_t grid = (int64_t)per_sm * device_sm_count();
   if (grid > a.M) grid = a.M;
@@ -85,7 +86,7 @@ static cudaError_t launch_f32_one(const F32Args& a, int threads, cudaStream_t st
   return cudaGetLastError();
 }
 
-cudaError_t launch_rmsnorm_f32(const F32Args& a, LaunchShape sh, cudaStream_t stream) {
+cudaError_t launch_rmsnorm_f32(const F32Args& a, F32Shape sh, cudaStream_t stream) {
   switch (sh.nv) {
     case 1: return launch_f32_one<1>(a, sh.threads, stream);
     case 2: return launch_f32_one<2>(a, sh.threads, stream);

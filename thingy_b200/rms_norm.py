@@ -22,10 +22,10 @@ def _threads_hint(threads_per_row: int | None, H: int) -> int:
     """The requested threads per row when this kernel can honour it, else 0 (auto)."""
     if not threads_per_row:
         return 0
-    V = H // 8
-    nv = max(1, -(-V // threads_per_row))
-    limit = 512 if nv > 4 else 1024
-    return threads_per_row if nv <= 8 and threads_per_row <= limit else 0
+    chunks = -(-H // 32)  # 64-byte chunks of a bf16 row
+    per_thread = max(1, -(-chunks // threads_per_row))
+    ok = per_thread == 1 or (per_thread == 2 and threads_per_row <= 512)
+    return threads_per_row if ok else 0
 
 
 class RMSNorm:
@@ -36,7 +36,8 @@ class RMSNorm:
     way its bench validates them (bench.py:166-188). This kernel always moves
     16-byte vectors and keeps the row in registers, so load_path and reduction
     do not change the result or the code path; threads_per_row is used as the
-    CTA size whenever it covers the row with at most 8 vectors per thread.
+    CTA size whenever it covers the row with one 64-byte chunk per thread (or
+    two, up to 512 threads).
 
     Keyword-only extensions select per-token (group_size=None), 1x32/1x64
     groups, power-of-two or e8m0 scales and column-major or swizzled layouts.
