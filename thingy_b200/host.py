@@ -121,8 +121,7 @@ def rms_norm_fp8_host(
                 scale=_scale_rows(s_dev, scale_layout, r0, r1, M, G),
                 residual_out=None if residual_out is None else p.res_out[k][:n],
                 group_size=group_size, scale_format=scale_format, scale_layout=scale_layout,
-                stream=p.s_run,
-            )
+            )  # on p.s_run, the current stream inside this block
             ev_used[k] = torch.cuda.Event()
             ev_used[k].record(p.s_run)
         with torch.cuda.stream(p.s_out):

@@ -3,7 +3,12 @@
 These are the destination-passing primitives every public entry point uses:
 the caller passes preallocated CUDA tensors, the work is enqueued on the
 current torch stream of the tensors' device (or on ``stream``), nothing is
-synchronised. Argument errors raise ValueError, CUDA failures CutieError.
+synchronised. Argument errors raise ValueError, CUDA failures RuntimeError.
+
+Calls go through the compiled torch binding (thingy_b200/_C, built next to
+the library) when it is present: it reads tensor metadata and the current
+stream in C++ and costs a few microseconds. Without it, or for a raw stream
+handle, the same C ABI is called through ctypes with the checks done here.
 """
 
 from __future__ import annotations
@@ -11,6 +16,11 @@ from __future__ import annotations
 import torch
 
 from . import _lib
+
+try:
+    from . import _C as _binding
+except ImportError:  # the ctypes path below covers the same entry points
+    _binding = None
 from .layouts import SCALE_FORMATS, SCALE_LAYOUTS, mx_swizzled_size, n_groups
 
 _FMT_CODE = {"fp32": _lib.SCALE_FP32, "ue8m0": _lib.SCALE_FP32_POW2, "e8m0": _lib.SCALE_E8M0}
@@ -123,12 +133,24 @@ def launch_rms_norm_fp8(
     ``q`` and ``scale`` both None means no quantization. ``group_size`` None
     (or 0) means one scale per row. ``normalize=False`` quantizes ``x`` as is.
     """
-    M, H = _check_x(x)
-    device = x.device
     if scale_format not in SCALE_FORMATS:
         raise ValueError(f"scale_format must be one of {SCALE_FORMATS}")
     if scale_layout not in SCALE_LAYOUTS:
         raise ValueError(f"scale_layout must be one of {SCALE_LAYOUTS}")
+    if _binding is not None and not isinstance(stream, int):
+        if not isinstance(x, torch.Tensor):
+            raise TypeError("x must be a torch.Tensor")
+        args = (x, weight, float(eps), residual, q, scale, residual_out, normalized_out,
+                int(group_size or 0), _FMT_CODE[scale_format], _LAYOUT_CODE[scale_layout],
+                int(threads_per_row), bool(normalize))
+        if stream is None:
+            _binding.rms_norm_fp8(*args)
+        else:
+            with torch.cuda.stream(stream):
+                _binding.rms_norm_fp8(*args)
+        return
+    M, H = _check_x(x)
+    device = x.device
     ldx = _rows("x", x, M, H, torch.bfloat16, device)
     ldr = _rows("residual", residual, M, H, torch.bfloat16, device) if residual is not None else 0
     ldro = (
@@ -191,6 +213,13 @@ def launch_rms_norm(
     stream=None,
 ) -> None:
     """Enqueue a standalone RMSNorm (bf16 or fp32, see include/cutie.h)."""
+    if _binding is not None and not isinstance(stream, int):
+        if stream is None:
+            _binding.rms_norm(x, weight, float(eps), out, int(threads_per_row))
+        else:
+            with torch.cuda.stream(stream):
+                _binding.rms_norm(x, weight, float(eps), out, int(threads_per_row))
+        return
     if x.dtype not in (torch.bfloat16, torch.float32):
         raise ValueError(f"x must be bfloat16 or float32, got {x.dtype}")
     M, H = _check_x(x, x.dtype)

@@ -12,6 +12,10 @@ bit for bit (parity tests build inputs on the CPU and copy them to the GPU).
   residual_token_32768x8192
                          residual add + per-token FP8, x ~ N(0,1),
                          residual ~ N(0, 4) (sigma 2), eps 1e-5, residual_out
+  rmsnorm_f32_MxH        the standalone fp32 RMSNorm of the reference's older
+                         baseline (x, w ~ N(0,1) fp32, eps 1e-5) at the shapes
+                         of its published sweep, M in {1024, 4096, 16384},
+                         H in {1024, 3072, 7168}
   mx32_decode_5120       decode-size MXFP8: M in {1, 8, 32, 128}, H 5120,
                          x ~ Student-t(nu=4), e8m0 scales per 32 elements in
                          the Blackwell swizzled layout, eps 1e-6
@@ -40,6 +44,7 @@ class Workload:
     scale_layout: str
     residual: bool
     dist: str  # "normal", "outliers", "student_t"
+    kind: str = "fused"  # "fused" (bf16 -> fp8) or "rms_f32" (standalone fp32 RMSNorm)
 
     def bytes_moved(self, M: int | None = None) -> int:
         """Algorithmic HBM bytes of one pass: inputs read once, outputs written once.
@@ -52,6 +57,8 @@ class Workload:
         """
         M = self.M if M is None else M
         H = self.H
+        if self.kind == "rms_f32":  # utils.py:10-19: x and out fp32, weight once
+            return 2 * M * H * 4 + H * 4
         groups = 1 if not self.group_size else -(-H // self.group_size)
         scale_bytes = 1 if self.scale_format == "e8m0" else 4
         total = 2 * M * H + 2 * H + M * H + scale_bytes * M * groups
@@ -70,6 +77,12 @@ WORKLOADS = {
         Workload("mx32_decode_5120", 128, 5120, 1e-6, 32, "e8m0", "mx", False, "student_t"),
         Workload("g128_sharded_262144x8192", 262144, 8192, 1e-6, 128, "fp32", "col", False,
                  "outliers"),
+        *(
+            Workload(f"rmsnorm_f32_{m}x{h}", m, h, 1e-5, None, "fp32", "row", False, "normal",
+                     kind="rms_f32")
+            for m in (1024, 4096, 16384)
+            for h in (1024, 3072, 7168)
+        ),
     )
 }
 
@@ -101,6 +114,11 @@ def make_inputs(w: Workload, M: int | None = None, *, device="cpu", seed: int = 
     H = w.H
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
+    if w.kind == "rms_f32":  # utils.py:38-59: randn x and weight, fp32
+        if row_offset:
+            gen.manual_seed(seed * 1_000_003 + row_offset)
+        x = torch.randn((M, H), generator=gen, device=device)
+        return {"x": x, "weight": torch.randn(H, generator=gen, device=device), "eps": w.eps}
     weight = _weight(H, gen, device)
     outliers = None
     if w.dist == "outliers":
