@@ -53,7 +53,7 @@ def test_exact_sum_bitexact(group_size, fmt, layout, residual, M, H):
 
 @pytest.mark.parametrize("group_size,fmt,layout", MODES)
 @pytest.mark.parametrize("residual", [False, True])
-@pytest.mark.parametrize("M,H", [(1000, 7168), (5000, 1024), (700, 8192), (2000, 5120)])
+@pytest.mark.parametrize("M,H", [(1000, 7168), (5000, 1024), (700, 8192), (2000, 5120), (1999, 4096)])
 def test_bulk_path_bitexact(group_size, fmt, layout, residual, M, H):
     """Batches of >= 4 rows per SM go through the bulk-copy ring (many rows per
     CTA, every stage reused several times, swizzle padding rows at the end)."""
