@@ -44,6 +44,17 @@ L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
 
 
+
+def _kernel_name(w, threads_per_row) -> str:
+    """The kernel that carries the timed step (the launch shape rules of csrc/capi.cu)."""
+    if w.kind == "rms_f32":
+        return "rmsnorm_f32_kernel"
+    if threads_per_row == 32:
+        return "rowwarp_rmsnorm_fp8_kernel"
+    if w.group_size is None:  # per-token scaling: the single-pass kernel
+        return "fused_rmsnorm_fp8_kernel"
+    return "pipe_rmsnorm_fp8_kernel"
+
 def parse_args():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawTextHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -397,7 +408,7 @@ def run_ours(args, rank, world, local_rank):
             "traffic": traffic,
             "traffic_source": traffic_src,
             "peak_source": peak_src,
-            "kernel": "rmsnorm_f32_kernel" if w.kind == "rms_f32" else "fused_rmsnorm_fp8_kernel",
+            "kernel": _kernel_name(w, args.threads_per_row),
             "bytes_per_launch": bytes_step,
             "mean_launch_ms": round(launch_ms_max, 5),
         },

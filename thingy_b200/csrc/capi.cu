@@ -148,6 +148,52 @@ BulkPlan plan_bulk(const void* kernel, int threads, int stage_bytes, int max_sta
   return plan;
 }
 
+BulkPlan plan_pipe(const void* kernel, int threads, int stage_bytes) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, BulkPlan> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t key = (reinterpret_cast<uint64_t>(kernel) * 0x9E3779B97F4A7C15ull) ^
+                       (static_cast<uint64_t>(threads) << 44) ^
+                       (static_cast<uint64_t>(stage_bytes) << 12) ^ static_cast<uint64_t>(dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  BulkPlan plan{0, 0, 0};
+  int sm_smem = 0, block_smem = 0, reserved = 0;
+  cudaFuncAttributes attr{};
+  if (cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev) !=
+          cudaSuccess ||
+      cudaDeviceGetAttribute(&block_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+          cudaSuccess ||
+      cudaDeviceGetAttribute(&reserved, cudaDevAttrReservedSharedMemoryPerBlock, dev) !=
+          cudaSuccess ||
+      cudaFuncGetAttributes(&attr, kernel) != cudaSuccess)
+    return plan;
+  const int by_regs = cached_blocks_per_sm(kernel, threads, 0);
+  int best = 0;
+  for (int stages = 3; stages >= 2; --stages) {
+    const int dyn = stages * stage_bytes;
+    if (dyn + (int)attr.sharedSizeBytes > block_smem) continue;
+    int b = sm_smem / (dyn + (int)attr.sharedSizeBytes + reserved);
+    if (b > by_regs) b = by_regs;
+    if (b * stages > best) {
+      best = b * stages;
+      plan = BulkPlan{stages, b, dyn};
+    }
+  }
+  if (plan.stages >= 2) {
+    const int n = set_smem_and_occupancy(kernel, threads, plan.smem_bytes);
+    if (n <= 0) plan = BulkPlan{0, 0, 0};
+    else plan.blocks_per_sm = n;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = plan;
+  return plan;
+}
+
 namespace {
 
 
@@ -178,18 +224,18 @@ int pick_shape(int64_t V, int64_t M, int requested, bool aliased, LaunchShape* o
                   "threads_per_row=%d leaves %lld 64-byte chunks per thread for a %lld-chunk "
                   "row (at most 1, or 2 with at most 512 threads)",
                   requested, (long long)nch, (long long)NC);
-    *out = {nch < 1 ? 1 : (int)nch, requested, false};
+    *out = {nch < 1 ? 1 : (int)nch, requested, false, nch <= 1};
     return CUTIE_OK;
   }
   int64_t T = (NC + 31) / 32 * 32;
   if (T < 32) T = 32;
   if (T <= 1024) {
-    *out = {1, (int)T, false};
+    *out = {1, (int)T, false, true};
     return CUTIE_OK;
   }
   T = ((NC + 1) / 2 + 31) / 32 * 32;
   if (T <= 512) {
-    *out = {2, (int)T, false};
+    *out = {2, (int)T, false, false};
     return CUTIE_OK;
   }
   if (!aliased) {  // wider rows than one CTA can hold: stream them per warp

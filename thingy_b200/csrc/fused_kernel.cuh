@@ -974,6 +974,7 @@ struct LaunchShape {
   int nch;      // single-pass kernel: 64-byte chunks per thread, 1 or 2
   int threads;  // single-pass kernel: threads per CTA (one row at a time)
   bool rowwarp; // use the warp-per-row two-pass kernel instead
+  bool pipe;    // nch == 1: prefer the pipelined kernel (pipe_kernel.cuh) where it applies
 };
 
 }  // namespace cutie

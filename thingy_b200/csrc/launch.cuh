@@ -4,6 +4,7 @@
 #pragma once
 
 #include "fused_kernel.cuh"
+#include "pipe_kernel.cuh"
 
 namespace cutie {
 
@@ -26,6 +27,10 @@ BulkPlan plan_bulk(const void* kernel, int threads, int stage_bytes, int max_sta
 int set_smem_and_occupancy(const void* kernel, int threads, int smem);
 
 constexpr int kMaxStages = 4;
+
+// Plan of the pipelined kernel: 2 or 3 stages a CTA, the most stages an SM
+// (CTAs x stages), deeper rings first on a tie. stages < 2: no plan.
+BulkPlan plan_pipe(const void* kernel, int threads, int stage_bytes);
 
 // Persistent grid: as many CTAs as can be resident, never more than rows.
 template <int NCH, int QM, int LPG, bool RES, bool NORM, bool FULL>
@@ -65,8 +70,59 @@ cudaError_t launch_rowwarp_one(FusedArgs a, cudaStream_t stream) {
   return cudaGetLastError();
 }
 
+// Pipelined kernel (pipe_kernel.cuh); *launched = false when two stages of
+// the row do not fit a CTA (the caller then runs the single-pass kernel).
+template <int QM, int LPG, bool RES, bool FULL, int SK, int MAXT>
+cudaError_t launch_pipe_one(FusedArgs a, int threads, cudaStream_t stream, bool* launched) {
+  auto kernel = pipe_rmsnorm_fp8_kernel<QM, LPG, RES, FULL, SK, MAXT>;
+  const int row_pad = (a.V * 16 + 63) / 64 * 64 + 64;
+  const int stage_bytes = row_pad * (RES ? 2 : 1);
+  const BulkPlan p = plan_pipe(reinterpret_cast<const void*>(kernel), threads, stage_bytes);
+  *launched = false;
+  if (p.stages < 2) return cudaSuccess;
+  a.stages = p.stages;
+  int64_t grid = (int64_t)p.blocks_per_sm * device_sm_count();
+  if (grid > a.M_pad) grid = a.M_pad;
+  *launched = true;
+  if (grid <= 0) return cudaSuccess;
+  kernel<<<(unsigned)grid, threads, p.smem_bytes, stream>>>(a);
+  return cudaGetLastError();
+}
+
+template <int QM, int LPG, bool RES, int SK>
+cudaError_t launch_pipe_sk(const FusedArgs& a, int threads, cudaStream_t stream, bool* launched) {
+  const bool full = (int64_t)threads * 4 == a.V;
+  if (threads <= 224)
+    return full ? launch_pipe_one<QM, LPG, RES, true, SK, 224>(a, threads, stream, launched)
+                : launch_pipe_one<QM, LPG, RES, false, SK, 224>(a, threads, stream, launched);
+  return full ? launch_pipe_one<QM, LPG, RES, true, SK, 1024>(a, threads, stream, launched)
+              : launch_pipe_one<QM, LPG, RES, false, SK, 1024>(a, threads, stream, launched);
+}
+
+template <int QM, int LPG, bool RES>
+cudaError_t launch_pipe(const FusedArgs& a, int threads, cudaStream_t stream, bool* launched) {
+  if constexpr (QM == kQNone) {
+    return launch_pipe_sk<QM, LPG, RES, kSkF32>(a, threads, stream, launched);
+  } else {
+    if (a.scale_layout == kLaySwizzled)
+      return launch_pipe_sk<QM, LPG, RES, kSkE8Swz>(a, threads, stream, launched);
+    switch (a.scale_fmt) {
+      case kFmtE8M0: return launch_pipe_sk<QM, LPG, RES, kSkE8>(a, threads, stream, launched);
+      case kFmtPow2: return launch_pipe_sk<QM, LPG, RES, kSkF32Pow2>(a, threads, stream, launched);
+      default: return launch_pipe_sk<QM, LPG, RES, kSkF32>(a, threads, stream, launched);
+    }
+  }
+}
+
 template <int QM, int LPG, bool RES, bool NORM>
 cudaError_t launch_fused_nch(const FusedArgs& a, LaunchShape sh, cudaStream_t stream) {
+  if constexpr (NORM && QM != kQToken) {
+    if (sh.pipe) {
+      bool launched = false;
+      const cudaError_t e = launch_pipe<QM, LPG, RES>(a, sh.threads, stream, &launched);
+      if (e != cudaSuccess || launched) return e;
+    }
+  }
   if (sh.rowwarp) {
     // no bounds predicates when the row is whole 2 KB pieces
     const bool full = a.V % 128 == 0;
