@@ -80,6 +80,38 @@ def test_random_parity(group_size, fmt, layout, residual):
     check_parity(inp, group_size, fmt, layout)
 
 
+@pytest.mark.parametrize("M,H", [(64, 4096), (300, 7168), (40, 1000)])
+def test_residual_add_extremes(M, H):
+    """bf16 + bf16 residual sums at the edges of the format: ties at bf16
+    precision, exponent gaps of 16+ bits, subnormal operands and sums, exact
+    cancellation. The kernels add bf16 pairs in one rounding; the reference
+    adds in fp32 and rounds to bf16; the two agree on every bf16 pair."""
+    g = torch.Generator().manual_seed(M + H)
+    sign = lambda *shape: torch.where(torch.rand(*shape, generator=g) < 0.5, -1.0, 1.0)
+    x = torch.randn(M, H, generator=g)
+    r = torch.randn(M, H, generator=g) * 2.0
+    c = torch.randint(0, 5, (M, H), generator=g)
+    one = sign(M, H) * 2.0 ** torch.randint(-10, 10, (M, H), generator=g).float()
+    ties = one * (1.0 + 2.0 ** -8 * torch.randint(1, 4, (M, H), generator=g).float())
+    x = torch.where(c == 0, one, x)
+    r = torch.where(c == 0, ties - one, r)  # x + r lands on or near a bf16 tie
+    tiny = sign(M, H) * 2.0 ** -133 * torch.randint(1, 127, (M, H), generator=g).float()
+    x = torch.where(c == 1, x * 2.0 ** 20, x)
+    r = torch.where(c == 1, tiny, r)  # exponent gap of 16+ bits
+    x = torch.where(c == 2, tiny, x)
+    r = torch.where(c == 2, -tiny * 0.5, r)  # subnormal operands and sums
+    r = torch.where(c == 3, -x, r)  # exact cancellation
+    inp = {
+        "x": x.to(torch.bfloat16),
+        "residual": r.to(torch.bfloat16),
+        "weight": (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16),
+        "eps": 1e-6,
+    }
+    assert (inp["residual"].float().abs() < 2.0 ** -126).any(), "no subnormal operands"
+    for gs, fmt, layout in [(128, "fp32", "col"), (32, "e8m0", "mx"), (None, "fp32", "row")]:
+        check_parity(inp, gs, fmt, layout)
+
+
 @pytest.mark.parametrize("H", [8, 16, 24, 200, 1000, 2048, 3072, 6144, 12288, 16384, 32768])
 def test_widths(H):
     """Every vectors-per-thread instantiation and ragged last groups."""

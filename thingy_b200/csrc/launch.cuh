@@ -83,6 +83,7 @@ cudaError_t launch_pipe_one(FusedArgs a, int threads, cudaStream_t stream, bool*
   a.stages = p.stages;
   int64_t grid = (int64_t)p.blocks_per_sm * device_sm_count();
   if (grid > a.M_pad) grid = a.M_pad;
+  if (grid > 0 && (a.M + grid - 1) / grid > INT32_MAX) return cudaSuccess;  // 32-bit row counter
   *launched = true;
   if (grid <= 0) return cudaSuccess;
   kernel<<<(unsigned)grid, threads, p.smem_bytes, stream>>>(a);

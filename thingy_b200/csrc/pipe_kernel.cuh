@@ -66,14 +66,27 @@ __device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
 
 // Wait for phase `parity`: one non-blocking test first (the phase has
 // usually completed), then suspending try_waits, giving up after
-// kWaitLimitCycles or when another warp of the CTA has given up.
+// kWaitLimitCycles or at once when the CTA's abort flag is set. A wait that
+// gives up sets the flag, so every later wait of the CTA returns at once.
 __device__ __forceinline__ bool mbar_wait_abortable(uint32_t bar, uint32_t parity,
-                                                    const volatile uint32_t* abort_flag) {
+                                                    volatile uint32_t* abort_flag) {
   if (mbar_test(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity))
-    if (*abort_flag || clock64() - t0 > kWaitLimitCycles) return false;
+  while (!mbar_try_wait(bar, parity)) {
+    if (*abort_flag || clock64() - t0 > kWaitLimitCycles) {
+      *abort_flag = 1u;
+      return false;
+    }
+  }
   return true;
+}
+
+// Streaming fp32 store guarded by `ok` inside the instruction (no branch).
+__device__ __forceinline__ void st_f32_if(bool ok, void* p, float v) {
+  asm volatile(
+      "{\n .reg .pred q;\n setp.ne.u32 q, %2, 0;\n @q st.global.f32 [%0], %1;\n}" ::"l"(p),
+      "f"(v), "r"((uint32_t)ok)
+      : "memory");
 }
 
 __device__ __forceinline__ uint32_t atom_add_acq_rel(uint32_t addr, uint32_t v) {
@@ -121,16 +134,18 @@ __device__ __forceinline__ void sq_acc(float2& acc, uint32_t u) {
       : "r"(u));
 }
 
+// Scale of one group, written by the group's leader lane (`put`).
 template <int SK>
-__device__ __forceinline__ void put_group_scale(const FusedArgs& a, int64_t row, char* srow,
-                                                int64_t goff, int g, float s) {
+__device__ __forceinline__ void put_group_scale(bool put, const FusedArgs& a, int64_t row,
+                                                char* srow, int64_t goff, int g, float s) {
   if constexpr (SK == kSkE8Swz) {
-    static_cast<uint8_t*>(a.scale)[swizzled_offset(row, g, a.n_groups_pad >> 2)] =
-        (uint8_t)(__float_as_uint(s) >> 23);
+    if (put)
+      static_cast<uint8_t*>(a.scale)[swizzled_offset(row, g, a.n_groups_pad >> 2)] =
+          (uint8_t)(__float_as_uint(s) >> 23);
   } else if constexpr (SK == kSkE8) {
-    srow[goff] = (char)(__float_as_uint(s) >> 23);
+    if (put) srow[goff] = (char)(__float_as_uint(s) >> 23);
   } else {
-    *reinterpret_cast<float*>(srow + goff) = s;
+    st_f32_if(put, srow + goff, s);
   }
 }
 
@@ -205,7 +220,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
       issued_cnt[s] = 0;
     }
     for (int k = 0; k < kPipeRing; ++k) {
-      mbar_init(smem_addr(&red_bar[k]), (uint32_t)nw);
+      mbar_init(smem_addr(&red_bar[k]), (uint32_t)T);  // every thread arrives
       mbar_init(smem_addr(&inv_bar[k]), 1);
     }
     abort_flag = 0;
@@ -226,7 +241,8 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   const int gidx = t / LPG;
   const int64_t goff = (int64_t)gidx * a.s_grp * kEsz;
   const bool gput = (t & (LPG - 1)) == 0 && (FULL || t * 4 < a.V);
-  const volatile uint32_t* abortp = &abort_flag;
+  volatile uint32_t* abortp = &abort_flag;
+  bool ok = true;  // every wait of this thread completed
 
   // Rings. Row k uses slot k & 3 of part/red_bar and of inv_slot/inv_bar.
   // Reuse is safe: a warp writes row k + 4's partial in phase A(k + 4),
@@ -236,10 +252,9 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   // same chain keeps any mbarrier from running two phases ahead of a waiter.
 
   // ---------------------------------------------------------------- phase A
-  auto phase_a = [&](int64_t k, int s, uint32_t par, uint8_t* rorow) -> bool {
+  auto phase_a = [&](int k, int s, uint32_t par, uint8_t* rorow) {
     const uint32_t base = ring + (uint32_t)s * stage_bytes;
-    const bool ok = mbar_wait_abortable(smem_addr(&full_bar[s]), par, abortp);
-    if (!__all_sync(0xffffffffu, ok)) return false;
+    ok &= mbar_wait_abortable(smem_addr(&full_bar[s]), par, abortp);
     uint32_t v[NV][4];
 #pragma unroll
     for (int k2 = 0; k2 < NV; ++k2) {
@@ -281,12 +296,11 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
 #pragma unroll
     for (int k2 = 1; k2 < NV; ++k2) acc[0] = __fadd2_rn(acc[0], acc[k2]);
     const float ss = warp_reduce<false>(__fadd_rn(acc[0].x, acc[0].y));
-    if (lane == 0) {
-      const int slot = (int)(k & (kPipeRing - 1));
-      part[slot][warp] = ss;
-      mbar_arrive(smem_addr(&red_bar[slot]));  // release: orders the store above
-    }
-    return true;
+    // every lane holds the warp's sum: all store it (one value) and arrive
+    // (release: orders the store before the arrival), no branch
+    const int slot = k & (kPipeRing - 1);
+    part[slot][warp] = ss;
+    mbar_arrive(smem_addr(&red_bar[slot]));
   };
 
   // ---------------------------------------------------------------- finisher
@@ -294,11 +308,10 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   // reciprocal square root; the double rounding is reproduced. The mean is
   // RN(ss / H) through the one-correction division (a quotient below the
   // normal range takes the IEEE one).
-  auto finalize = [&](int64_t k) -> bool {
-    const int slot = (int)(k & (kPipeRing - 1));
+  auto finalize = [&](int k) {
+    const int slot = k & (kPipeRing - 1);
     const uint32_t par = (uint32_t)(k >> 2) & 1u;
-    const bool ok = mbar_wait_abortable(smem_addr(&red_bar[slot]), par, abortp);
-    if (!__all_sync(0xffffffffu, ok)) return false;
+    ok &= mbar_wait_abortable(smem_addr(&red_bar[slot]), par, abortp);
     const float total = combine_partials<false>(part[slot], lane, nw);
     float mean = div_rn(total, (float)a.H, a.rcp_H);
     if (mean < 0x1p-100f) mean = __fdiv_rn(total, (float)a.H);
@@ -306,16 +319,14 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
       inv_slot[slot] = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, a.eps)));
       mbar_arrive(smem_addr(&inv_bar[slot]));
     }
-    return true;
   };
 
   // ---------------------------------------------------------------- phase B
-  auto phase_b = [&](int64_t k, int s, uint32_t use, int64_t row, uint8_t* qrow, char* srow,
-                     uint8_t* norow) -> bool {
-    const int slot = (int)(k & (kPipeRing - 1));
+  auto phase_b = [&](int k, int s, uint32_t use, int64_t row, uint8_t* qrow, char* srow,
+                     uint8_t* norow) {
+    const int slot = k & (kPipeRing - 1);
     const uint32_t par = (uint32_t)(k >> 2) & 1u;
-    const bool ok = mbar_wait_abortable(smem_addr(&inv_bar[slot]), par, abortp);
-    if (!__all_sync(0xffffffffu, ok)) return false;
+    ok &= mbar_wait_abortable(smem_addr(&inv_bar[slot]), par, abortp);
     const float inv = inv_slot[slot];
     const uint32_t base = ring + (uint32_t)s * stage_bytes;
     uint32_t v[NV][4];
@@ -375,7 +386,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
       const float sc = make_scale(__uint_as_float(p << 16), kPow2);
       // a power-of-two scale has an exact reciprocal: negate the exponent
       const float rc = kPow2 ? __uint_as_float((254u << 23) - __float_as_uint(sc)) : __frcp_rn(sc);
-      if (gput) put_group_scale<SK>(a, row, srow, goff, gidx, sc);
+      put_group_scale<SK>(gput, a, row, srow, goff, gidx, sc);
       if constexpr (SK == kSkE8Swz)
         if (a.n_groups_pad > a.n_groups) zero_scale_padding(a, row, a.n_groups, t, T);
       const float2 rc2 = make_float2(rc, rc), nb = make_float2(-sc, -sc);
@@ -396,7 +407,6 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
           st_stream2_if(vok[k2], qrow + (voff[k2] >> 1), c0, c1);
       }
     }
-    return true;
   };
 
   // ------------------------------------------------------------ main loop
@@ -406,27 +416,29 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   char* srow = static_cast<char*>(a.scale) + (int64_t)blockIdx.x * a.s_row * kEsz;
   uint8_t* norow = reinterpret_cast<uint8_t*>(a.norm_out) + (int64_t)blockIdx.x * a.ldn * 2;
   uint8_t* rorow = reinterpret_cast<uint8_t*>(a.res_out) + (int64_t)blockIdx.x * a.ldro * 2;
-  bool ok = true;
-  int sB = 0, sA = 0;        // stages of rows k (phase B) and k + 1 (phase A)
+  int sB = 0, sA = 0;           // stages of rows k (phase B) and k + 1 (phase A)
   uint32_t useB = 0, useA = 0;  // how many times the ring wrapped at those rows
-  int fin = 0;               // k % nw
-  if (nrows > 0) {
-    ok = phase_a(0, 0, 0u, rorow);
+  int fin = 0;                  // k % nw
+  const int nr = (int)nrows;    // the host keeps rows per CTA below 2^31
+  if (nr > 0) {
+    phase_a(0, 0, 0u, rorow);
     rorow += r_step;
   }
   int64_t row = blockIdx.x;
-  for (int64_t k = 0; ok && k < nrows; ++k, row += G) {
-    if (warp == fin) ok = finalize(k);
+  // A failed wait does not branch out of a phase (the rows it touches are
+  // garbage, never out of bounds); the warp leaves at the end of the row.
+  for (int k = 0; k < nr; ++k, row += G) {
+    if (warp == fin) finalize(k);
     if (++fin == nw) fin = 0;
     if (++sA == S) {
       sA = 0;
       ++useA;
     }
-    if (ok && k + 1 < nrows) {
-      ok = phase_a(k + 1, sA, useA & 1u, rorow);
+    if (k + 1 < nr) {
+      phase_a(k + 1, sA, useA & 1u, rorow);
       rorow += r_step;
     }
-    if (ok) ok = phase_b(k, sB, useB, row, qrow, srow, norow);
+    phase_b(k, sB, useB, row, qrow, srow, norow);
     if (++sB == S) {
       sB = 0;
       ++useB;
@@ -434,7 +446,9 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
     qrow += q_step;
     srow += s_step;
     norow += n_step;
+    if (!__all_sync(0xffffffffu, ok)) break;
   }
+  ok = __all_sync(0xffffffffu, ok);
   if (!ok && lane == 0) {
     atomicCAS(&g_cutie_device_error, kDevErrNone, kDevErrBulkWaitTimeout);
     abort_flag = 1u;
