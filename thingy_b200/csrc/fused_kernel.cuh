@@ -180,6 +180,75 @@ __device__ __forceinline__ void st_stream2_if(bool ok, void* p, uint32_t a, uint
       : "memory");
 }
 
+// 32-byte streaming store (one full sector), address 32-byte aligned.
+__device__ __forceinline__ void st_stream8(void* p, const uint32_t* v) {
+  asm volatile("st.global.cs.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v[0]),
+               "r"(v[1]), "r"(v[2]), "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
+// ------------------------------------------------- natural-order chunk stores
+//
+// A thread visits the 4 vectors of its 64-byte chunk in a rotated order (slot
+// k holds vector (k + rot) & 3; see the kernels). Stored in that order, every
+// store instruction of a warp covers each 32-byte sector of the output only
+// partly. These helpers put a chunk back in vector order and store it as
+// whole sectors: 32 e4m3 codes are one 32-byte sector, 32 bf16 values two.
+
+// slots c[b .. b+3] -> vector order: d[j] = c[b + ((j - rot) & 3)], two selects
+// per word (b: the chunk's first slot, a constant after unrolling)
+template <int W, int N>
+__device__ __forceinline__ void unrotate_chunk(const uint32_t (&c)[N][W], int b, int rot,
+                                               uint32_t (&d)[4 * W]) {
+  const bool r1 = (rot & 1) != 0, r2 = (rot & 2) != 0;
+  uint32_t e[4][W];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+#pragma unroll
+    for (int i = 0; i < W; ++i) e[k][i] = r2 ? c[b + ((k + 2) & 3)][i] : c[b + k][i];
+#pragma unroll
+  for (int j = 0; j < 4; ++j)
+#pragma unroll
+    for (int i = 0; i < W; ++i) d[W * j + i] = r1 ? e[(j + 3) & 3][i] : e[j][i];
+}
+
+// 32 codes of one chunk at p (chunk's first vector index vfirst, row of V
+// vectors). a32 / a16: p is 32- / 16-byte aligned.
+template <bool FULL>
+__device__ __forceinline__ void store_chunk_codes(uint8_t* p, const uint32_t (&d)[8], bool a32,
+                                                  bool a16, int vfirst, int V) {
+  if (FULL && a32) {
+    st_stream8(p, d);
+  } else if (FULL && a16) {
+    const uint32_t lo[4] = {d[0], d[1], d[2], d[3]}, hi[4] = {d[4], d[5], d[6], d[7]};
+    st_stream(p, lo);
+    st_stream(p + 16, hi);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) st_stream2_if(FULL || vfirst + j < V, p + 8 * j, d[2 * j], d[2 * j + 1]);
+  }
+}
+
+// 32 bf16 values of one chunk at p (16-byte aligned; a32: 32-byte aligned)
+template <bool FULL>
+__device__ __forceinline__ void store_chunk_bf16(uint8_t* p, const uint32_t (&d)[16], bool a32,
+                                                 int vfirst, int V) {
+  if (FULL && a32) {
+    st_stream8(p, d);
+    st_stream8(p + 32, d + 8);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const uint32_t q[4] = {d[4 * j], d[4 * j + 1], d[4 * j + 2], d[4 * j + 3]};
+      st_stream_if(FULL || vfirst + j < V, p + 16 * j, q);
+    }
+  }
+}
+
+__device__ __forceinline__ bool aligned_rows(const void* p, int64_t ld_bytes, unsigned n) {
+  return ((reinterpret_cast<uint64_t>(p) | (uint64_t)ld_bytes) & (n - 1u)) == 0;
+}
+
 // ------------------------------------------------- mbarrier + bulk copies
 
 __device__ __forceinline__ uint32_t smem_addr(const void* p) {
@@ -444,6 +513,10 @@ __global__ void __launch_bounds__(NCH == 1 ? 1024 : 512) fused_rmsnorm_fp8_kerne
   const bool pow2 = a.scale_fmt != kFmtF32;
   const bool store_ro = RES && a.res_out != nullptr;
   const bool store_no = NORM && a.norm_out != nullptr;
+  // output rows on 32- / 16-byte boundaries take whole-sector stores
+  const bool q32 = aligned_rows(a.q, a.ldq, 32), q16 = aligned_rows(a.q, a.ldq, 16);
+  const bool ro32 = aligned_rows(a.res_out, a.ldro * 2, 32);
+  const bool no32 = aligned_rows(a.norm_out, a.ldn * 2, 32);
   // Row pointers advance by G rows per iteration.
   const int esz = a.scale_fmt == kFmtE8M0 ? 1 : 4;
   uint8_t* qrow = a.q + (int64_t)blockIdx.x * a.ldq;
@@ -490,11 +563,11 @@ __global__ void __launch_bounds__(NCH == 1 ? 1024 : 512) fused_rmsnorm_fp8_kerne
       }
       if (store_ro) {
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          if constexpr (FULL)
-            st_stream(rorow + voff[k], v[k]);
-          else
-            st_stream_if(vok[k], rorow + voff[k], v[k]);
+        for (int c = 0; c < NCH; ++c) {
+          uint32_t d[16];
+          unrotate_chunk(v, 4 * c, rot, d);
+          const int ch = c * T + t;
+          store_chunk_bf16<FULL>(rorow + 64 * ch, d, ro32, 4 * ch, a.V);
         }
       }
     }
@@ -589,11 +662,11 @@ __global__ void __launch_bounds__(NCH == 1 ? 1024 : 512) fused_rmsnorm_fp8_kerne
           v[k][j] = mul_bf2(f2_to_bf2(__fmul2_rn(bf2_to_f2(v[k][j]), inv2)), w[k][j]);
       if (store_no) {
 #pragma unroll
-        for (int k = 0; k < NV; ++k) {
-          if constexpr (FULL)
-            st_stream(norow + voff[k], v[k]);
-          else
-            st_stream_if(vok[k], norow + voff[k], v[k]);
+        for (int c = 0; c < NCH; ++c) {
+          uint32_t d[16];
+          unrotate_chunk(v, 4 * c, rot, d);
+          const int ch = c * T + t;
+          store_chunk_bf16<FULL>(norow + 64 * ch, d, no32, 4 * ch, a.V);
         }
       }
     }
@@ -656,6 +729,7 @@ __global__ void __launch_bounds__(NCH == 1 ? 1024 : 512) fused_rmsnorm_fp8_kerne
         }
         if (t == 0) store_scale(a, row, 0, s1);
       }
+      uint32_t cw[NV][2];
 #pragma unroll
       for (int k = 0; k < NV; ++k) {
         const float2 rc2 = make_float2(rc[k >> 2], rc[k >> 2]);
@@ -668,11 +742,15 @@ __global__ void __launch_bounds__(NCH == 1 ? 1024 : 512) fused_rmsnorm_fp8_kerne
 #pragma unroll
           for (int j = 0; j < 4; ++j) y[j] = div2_rn(bf2_to_f2(v[k][j]), nb, rc2);
         }
-        const uint32_t c0 = f4_to_e4m3x4(y[0], y[1]), c1 = f4_to_e4m3x4(y[2], y[3]);
-        if constexpr (FULL)
-          st_stream2(qrow + (voff[k] >> 1), c0, c1);
-        else
-          st_stream2_if(vok[k], qrow + (voff[k] >> 1), c0, c1);
+        cw[k][0] = f4_to_e4m3x4(y[0], y[1]);
+        cw[k][1] = f4_to_e4m3x4(y[2], y[3]);
+      }
+#pragma unroll
+      for (int c = 0; c < NCH; ++c) {
+        uint32_t d[8];
+        unrotate_chunk(cw, 4 * c, rot, d);
+        const int ch = c * T + t;
+        store_chunk_codes<FULL>(qrow + 32 * ch, d, q32, q16, 4 * ch, a.V);
       }
     }
   }

@@ -243,6 +243,8 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   const bool gput = (t & (LPG - 1)) == 0 && (FULL || t * 4 < a.V);
   volatile uint32_t* abortp = &abort_flag;
   bool ok = true;  // every wait of this thread completed
+  // code rows on 32- (16-) byte boundaries take one 32-byte store a thread
+  const bool q32 = aligned_rows(a.q, a.ldq, 32), q16 = aligned_rows(a.q, a.ldq, 16);
 
   // Rings. Row k uses slot k & 3 of part/red_bar and of inv_slot/inv_bar.
   // Reuse is safe: a warp writes row k + 4's partial in phase A(k + 4),
@@ -390,6 +392,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
       if constexpr (SK == kSkE8Swz)
         if (a.n_groups_pad > a.n_groups) zero_scale_padding(a, row, a.n_groups, t, T);
       const float2 rc2 = make_float2(rc, rc), nb = make_float2(-sc, -sc);
+      uint32_t cw[NV][2];
 #pragma unroll
       for (int k2 = 0; k2 < NV; ++k2) {
         float2 y[4];
@@ -400,12 +403,13 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
           else
             y[j] = div2_rn(bf2_to_f2(v[k2][j]), nb, rc2);
         }
-        const uint32_t c0 = f4_to_e4m3x4(y[0], y[1]), c1 = f4_to_e4m3x4(y[2], y[3]);
-        if constexpr (FULL)
-          st_stream2(qrow + (voff[k2] >> 1), c0, c1);
-        else
-          st_stream2_if(vok[k2], qrow + (voff[k2] >> 1), c0, c1);
+        cw[k2][0] = f4_to_e4m3x4(y[0], y[1]);
+        cw[k2][1] = f4_to_e4m3x4(y[2], y[3]);
       }
+      // back to vector order, whole 32-byte sectors where the rows allow
+      uint32_t d[8];
+      unrotate_chunk(cw, 0, rot, d);
+      store_chunk_codes<FULL>(qrow + 32 * t, d, q32, q16, 4 * t, a.V);
     }
   };
 
