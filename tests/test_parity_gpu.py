@@ -386,3 +386,38 @@ def test_division_matches_ieee_on_gpu():
     # reciprocal, which is not the IEEE quotient
     s_ieee = torch.clamp(am.cuda() / torch.full_like(am, 448.0).cuda(), min=1e-4).view(rows, 16)
     assert torch.equal(s, s_ieee)
+
+
+@pytest.mark.parametrize("M,H", [(16384, 7168), (64, 5120), (4096, 4096)])
+def test_back_to_back_launches_see_previous_outputs(M, H):
+    """Kernels start their prologue while the previous kernel drains
+    (programmatic dependent launch); each must still read only complete
+    outputs of the kernel before it. A chain where every launch consumes the
+    previous launch's normalized output and residual sum, enqueued back to
+    back on one stream, must equal the same chain run with a synchronize
+    between the steps."""
+    g = torch.Generator().manual_seed(M + H)
+    dev = torch.device("cuda")
+    x = torch.randn(M, H, generator=g).to(torch.bfloat16).to(dev)
+    r = (2.0 * torch.randn(M, H, generator=g)).to(torch.bfloat16).to(dev)
+    w = (1.0 + 0.1 * torch.randn(H, generator=g)).to(torch.bfloat16).to(dev)
+
+    def chain(sync):
+        cur_x, cur_r, outs = x, r, []
+        for _ in range(6):
+            q, s, ro, n = tb.rms_norm_fp8(cur_x, w, 1e-6, residual=cur_r, group_size=128,
+                                          scale_format="fp32", scale_layout="col",
+                                          return_normalized=True)
+            outs.append((q, s))
+            cur_x, cur_r = n, ro  # the next launch reads this launch's outputs
+            if sync:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        return outs
+
+    ref = chain(True)
+    for _ in range(3):
+        got = chain(False)
+        for (q0, s0), (q1, s1) in zip(ref, got):
+            assert torch.equal(q0.view(torch.uint8), q1.view(torch.uint8))
+            assert torch.equal(s0, s1)

@@ -125,6 +125,21 @@ __device__ __forceinline__ uint32_t f4_to_e4m3x4(float2 a, float2 b) {
   return r;
 }
 
+// ------------------------------------------------- programmatic dependent launch
+//
+// Kernels here are launched with programmatic stream serialization: the next
+// kernel of the stream may be scheduled as soon as every CTA of the current
+// one has called griddep_launch_dependents(), and runs its prologue (shared
+// memory and barrier set-up) while the current one drains. Every kernel calls
+// griddep_wait() before its first global-memory access; it returns once the
+// preceding grid has completed and its writes are visible, so inputs written
+// by the previous kernel are never read early. Without the launch attribute
+// both are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ------------------------------------------------------------ memory helpers
 
 // Read-only cached load (weights are shared by every row).
@@ -504,6 +519,8 @@ __global__ void __launch_bounds__(NCH == 1 ? 1024 : 512) fused_rmsnorm_fp8_kerne
     mbar_init_fence();
   }
   __syncthreads();
+  griddep_wait();  // inputs of the previous kernel are complete from here on
+  griddep_launch_dependents();
   if (t == 0)
     for (int s = 0; s < S; ++s) {
       const int64_t row = blockIdx.x + (int64_t)s * G;
@@ -864,6 +881,8 @@ __global__ void __launch_bounds__(kRowwarpWarps * 32, RES ? 6 : 8)
     mbar_init_fence();
   }
   __syncwarp();
+  griddep_wait();  // inputs of the previous kernel are complete from here on
+  griddep_launch_dependents();
   if (lane == 0)
     while (iss < total && iss < P) issue_next();
 

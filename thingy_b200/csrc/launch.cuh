@@ -28,6 +28,25 @@ int set_smem_and_occupancy(const void* kernel, int threads, int smem);
 
 constexpr int kMaxStages = 4;
 
+// Launch with programmatic stream serialization (see griddep_wait in
+// fused_kernel.cuh): the kernel's prologue may overlap the previous kernel's
+// tail; its global accesses still wait for that kernel to complete.
+template <class... P, class... A>
+cudaError_t launch_pdl(void (*kernel)(P...), unsigned grid, unsigned block, size_t smem,
+                       cudaStream_t stream, A&&... args) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(grid);
+  cfg.blockDim = dim3(block);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, static_cast<A&&>(args)...);
+}
+
 // Plan of the pipelined kernel: 2 or 3 stages a CTA, the most stages an SM
 // (CTAs x stages), deeper rings first on a tie. stages < 2: no plan.
 BulkPlan plan_pipe(const void* kernel, int threads, int stage_bytes);
@@ -45,8 +64,7 @@ cudaError_t launch_fused_one(FusedArgs a, int threads, cudaStream_t stream) {
   int64_t grid = (int64_t)p.blocks_per_sm * device_sm_count();
   if (grid > a.M_pad) grid = a.M_pad;
   if (grid <= 0) return cudaSuccess;
-  kernel<<<(unsigned)grid, threads, p.smem_bytes, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(kernel, (unsigned)grid, (unsigned)threads, (size_t)p.smem_bytes, stream, a);
 }
 
 // Warp-per-row kernel: kRowwarpWarps warps per CTA, a private ring of
@@ -66,8 +84,7 @@ cudaError_t launch_rowwarp_one(FusedArgs a, cudaStream_t stream) {
   const int64_t need = (a.M_pad + kRowwarpWarps - 1) / kRowwarpWarps;
   if (grid > need) grid = need;
   if (grid <= 0) return cudaSuccess;
-  kernel<<<(unsigned)grid, kThreads, smem, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(kernel, (unsigned)grid, (unsigned)kThreads, (size_t)smem, stream, a);
 }
 
 // Pipelined kernel (pipe_kernel.cuh); *launched = false when two stages of
@@ -86,8 +103,7 @@ cudaError_t launch_pipe_one(FusedArgs a, int threads, cudaStream_t stream, bool*
   if (grid > 0 && (a.M + grid - 1) / grid > INT32_MAX) return cudaSuccess;  // 32-bit row counter
   *launched = true;
   if (grid <= 0) return cudaSuccess;
-  kernel<<<(unsigned)grid, threads, p.smem_bytes, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(kernel, (unsigned)grid, (unsigned)threads, (size_t)p.smem_bytes, stream, a);
 }
 
 template <int QM, int LPG, bool RES, int SK>

@@ -227,6 +227,8 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
     mbar_init_fence();
   }
   __syncthreads();
+  griddep_wait();  // inputs of the previous kernel are complete from here on
+  griddep_launch_dependents();
   if (t == 0)
     for (int s = 0; s < S && s < nrows; ++s) {
       issued_cnt[s] = 1;

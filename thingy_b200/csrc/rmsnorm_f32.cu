@@ -17,6 +17,8 @@ __global__ void __launch_bounds__(NV > 4 ? 512 : 1024) rmsnorm_f32_kernel(const 
   const int lane = t & 31, warp = t >> 5, nw = T >> 5;
   int flip = 0;
 
+  griddep_wait();  // inputs of the previous kernel are complete from here on
+  griddep_launch_dependents();
   float4 w[NV];
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
@@ -82,8 +84,7 @@ static cudaError_t launch_f32_one(const F32Args& a, int threads, cudaStream_t st
   int64_t grid = (int64_t)per_sm * device_sm_count();
   if (grid > a.M) grid = a.M;
   if (grid <= 0) return cudaSuccess;
-  kernel<<<(unsigned)grid, threads, 0, stream>>>(a);
-  return cudaGetLastError();
+  return launch_pdl(kernel, (unsigned)grid, (unsigned)threads, (size_t)0, stream, a);
 }
 
 cudaError_t launch_rmsnorm_f32(const F32Args& a, F32Shape sh, cudaStream_t stream) {
