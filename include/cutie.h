@@ -150,7 +150,9 @@ CUTIE_API int cutie_rms_norm(const void* x, int64_t ldx, const void* weight, flo
  * no kernel has hit a failure since the last clear; otherwise the first error
  * code recorded (1 = a bulk-copy wait ran out: a row never arrived in shared
  * memory within ~2 s and the kernel stopped early, leaving outputs
- * incomplete). Synchronises with the device; `clear` != 0 resets the word.
+ * incomplete; 2 = a kernel was launched with a shared-memory ring depth it
+ * does not hold and wrote nothing). Synchronises with the device; `clear` != 0
+ * resets the word.
  * A negative return is a CUDA failure (see cutie_last_error()).
  */
 CUTIE_API int cutie_device_error(int clear);

@@ -42,7 +42,7 @@ enum : int { kLayStrided = 0, kLaySwizzled = 1 };
 // failure; read and cleared through cutie_device_error(). Each translation
 // unit that launches kernels has its own copy (internal linkage, no
 // relocatable device code needed); the host side reads all of them.
-enum : int { kDevErrNone = 0, kDevErrBulkWaitTimeout = 1 };
+enum : int { kDevErrNone = 0, kDevErrBulkWaitTimeout = 1, kDevErrBadLaunch = 2 };
 static __device__ int g_cutie_device_error = 0;
 
 // Every pointer is device memory; bf16 tensors are passed as raw 16-bit words.

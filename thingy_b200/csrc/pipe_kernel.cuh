@@ -208,6 +208,13 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
     if constexpr (RES) bulk_g2s(dst + row_pad, a.res + row * a.ldr, row_bytes, bar);
   };
 
+  // the barrier and counter arrays hold kPipeMaxStages stages; the host plans
+  // 2-3 (a plan outside [2, kPipeMaxStages] is refused before any set-up)
+  if (S < 2 || S > kPipeMaxStages) {
+    if (t == 0) atomicCAS(&g_cutie_device_error, kDevErrNone, kDevErrBadLaunch);
+    return;
+  }
+
   // zero the pad of every row buffer once (the copies never write it)
   for (int s = 0; s < S * (RES ? 2 : 1); ++s)
     for (uint32_t b = row_bytes + 4u * (uint32_t)t; b < row_pad; b += 4u * (uint32_t)T)
