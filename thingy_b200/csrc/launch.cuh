@@ -92,7 +92,7 @@ cudaError_t launch_rowwarp_one(FusedArgs a, cudaStream_t stream) {
 template <int QM, int LPG, bool RES, bool FULL, int SK, int MAXT>
 cudaError_t launch_pipe_one(FusedArgs a, int threads, cudaStream_t stream, bool* launched) {
   auto kernel = pipe_rmsnorm_fp8_kernel<QM, LPG, RES, FULL, SK, MAXT>;
-  const int row_pad = (a.V * 16 + 63) / 64 * 64 + 64;
+  const int row_pad = (int)pipe_row_pad(a.V, threads, PipeLayout<QM, LPG>::kInterleaved);
   const int stage_bytes = row_pad * (RES ? 2 : 1);
   const BulkPlan p = plan_pipe(reinterpret_cast<const void*>(kernel), threads, stage_bytes);
   *launched = false;

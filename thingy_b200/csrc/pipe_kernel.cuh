@@ -2,9 +2,12 @@
 // FP8 quantization | no quantization], the default path for rows that fit
 // one CTA (H <= 32768).
 //
-// Same arithmetic, bit for bit, as fused_rmsnorm_fp8_kernel (fused_kernel.cuh)
-// and the same chunk layout (64-byte chunks, one per thread, rotated reads);
-// what changes is how a CTA moves from row to row. The single-pass kernel
+// Same per-element arithmetic as fused_rmsnorm_fp8_kernel (fused_kernel.cuh);
+// for 1x32 and 1x64 groups also the same chunk layout (64-byte chunks, one
+// per thread, rotated reads) and so the same bits. 1x128 groups and plain
+// RMSNorm output use an interleaved layout (below) whose sum of squares adds
+// the same terms in another order. What changes most is how a CTA moves from
+// row to row. The single-pass kernel
 // stops every warp at two block barriers per row. Here nothing waits on a
 // block barrier inside the row loop:
 //
@@ -149,19 +152,49 @@ __device__ __forceinline__ void put_group_scale(bool put, const FusedArgs& a, in
   }
 }
 
+// Thread layouts. Every thread holds 4 vectors (32 elements) of a row.
+//  * chunked (1x32 and 1x64 groups): the 4 vectors are one contiguous 64-byte
+//    chunk, so a 1x32 group is one thread and a 1x64 group two lanes; the
+//    chunk is visited in a per-thread rotated order (see fused_kernel.cuh).
+//  * interleaved (1x128 groups and no quantization): lane i of octet o of
+//    warp w holds vectors w*128 + o*32 + i + 8k, k = 0..3. The 8 lanes of an
+//    octet read 128 contiguous bytes per vector slot (conflict-free shared
+//    loads, and whole 32-byte sectors per store), every address is the
+//    thread's base plus a constant, and an octet covers two 1x128 groups:
+//    slots 0-1 are the first, slots 2-3 the second.
+template <int QM, int LPG>
+struct PipeLayout {
+  static constexpr bool kInterleaved = QM == kQNone || LPG == 4;
+};
+
+// Bytes of one row buffer in shared memory: the copied row plus a zero pad
+// that every vector slot past the row end reads. Chunked: whole chunks plus
+// one more zero chunk; interleaved: T * 64 bytes (4 vectors a thread).
+__host__ __device__ inline uint32_t pipe_row_pad(int V, int T, bool interleaved) {
+  const uint32_t row_bytes = (uint32_t)V * 16u;
+  if (interleaved) {
+    const uint32_t span = (uint32_t)T * 64u;
+    return span > row_bytes ? span : row_bytes;
+  }
+  return ((row_bytes + 63u) & ~63u) + 64u;
+}
+
 // QM: kQGroup (LPG lanes a group) or kQNone. FULL: T * 4 == V (no store
 // predicates). SK: scale destination. MAXT: the largest block this
 // instantiation is launched with; 224 lets the compiler use 72 registers a
-// thread (four 7-warp CTAs an SM), 1024 caps it at 64.
+// thread (four 7-warp CTAs an SM), 1024 caps it at 64. (A 56-register cap
+// for five CTAs an SM measured slower: the extra warps did not raise the
+// issue rate, and the cap added instructions.)
 //
-// Dynamic shared memory: `a.stages` stages of [x row | residual row], the
-// layout of the single-pass kernel (row buffers padded with a zero chunk).
+// Dynamic shared memory: `a.stages` stages of [x row | residual row], each
+// row buffer pipe_row_pad() bytes.
 template <int QM, int LPG, bool RES, bool FULL, int SK, int MAXT>
 __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
     pipe_rmsnorm_fp8_kernel(const FusedArgs a) {
   static_assert(QM == kQGroup || QM == kQNone, "group or no quantization");
   static_assert(QM != kQGroup || LPG == 1 || LPG == 2 || LPG == 4, "lanes per group");
-  constexpr int NV = 4;  // one 64-byte chunk (4 vectors) a thread
+  constexpr int NV = 4;  // 4 vectors (32 elements) a thread
+  constexpr bool ILV = PipeLayout<QM, LPG>::kInterleaved;
   constexpr bool kPow2 = SK != kSkF32;
   constexpr int kEsz = (SK == kSkE8 || SK == kSkE8Swz) ? 1 : 4;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -180,24 +213,33 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   const int S = a.stages;
   const uint32_t row_bytes = (uint32_t)a.V * 16u;
   const uint32_t row_chunks = (row_bytes + 63u) & ~63u;
-  const uint32_t row_pad = row_chunks + 64u;
+  const uint32_t row_pad = pipe_row_pad(a.V, T, ILV);
   const uint32_t stage_bytes = RES ? 2u * row_pad : row_pad;
   const uint32_t ring = smem_addr(smem);
   const int64_t G = gridDim.x;
   const int64_t nrows = (int64_t)blockIdx.x < a.M ? (a.M - 1 - blockIdx.x) / G + 1 : 0;
 
-  // Byte offset of this thread's k-th vector within a row, as in the
-  // single-pass kernel (vector j of the chunk visited at (j + rot) & 3).
+  // Byte offset of this thread's k-th vector within a row (voff[k], or
+  // tvec * 16 + 128 k interleaved) and whether it lies inside the row.
+  // Chunked: vector j of the chunk is visited at (j + rot) & 3, as in the
+  // single-pass kernel.
   const int rot = (t >> 1) & 3;
+  const int tvec = warp * 128 + (lane >> 3) * 32 + (lane & 7);  // interleaved: slot 0
+  const uint32_t toff = (uint32_t)tvec * 16u;
   uint32_t voff[NV];
   bool vok[NV];
 #pragma unroll
   for (int k = 0; k < NV; ++k) {
-    const int j = (k + rot) & 3;
-    const int vi = t * 4 + j;
-    vok[k] = FULL || vi < a.V;
-    voff[k] = FULL || (uint32_t)t * 64u < row_chunks ? (uint32_t)vi * 16u
-                                                      : row_chunks + 16u * (uint32_t)j;
+    if constexpr (ILV) {
+      vok[k] = FULL || tvec + 8 * k < a.V;
+      voff[k] = toff + 128u * (uint32_t)k;
+    } else {
+      const int j = (k + rot) & 3;
+      const int vi = t * 4 + j;
+      vok[k] = FULL || vi < a.V;
+      voff[k] = FULL || (uint32_t)t * 64u < row_chunks ? (uint32_t)vi * 16u
+                                                        : row_chunks + 16u * (uint32_t)j;
+    }
   }
 
   auto issue = [&](int s, int64_t row) {
@@ -246,10 +288,12 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   const bool store_no = a.norm_out != nullptr;
   const uint8_t* wbase = reinterpret_cast<const uint8_t*>(a.w);
   // this thread's group: index, byte offset within a strided scale row, and
-  // whether it writes the scale (leader lane of a group inside the row)
-  const int gidx = t / LPG;
+  // whether it writes the scale (leader lane of a group inside the row;
+  // interleaved: lanes 0 and 1 of each octet, for its two groups)
+  const int gidx = ILV ? warp * 8 + (lane >> 3) * 2 + (lane & 1) : t / LPG;
   const int64_t goff = (int64_t)gidx * a.s_grp * kEsz;
-  const bool gput = (t & (LPG - 1)) == 0 && (FULL || t * 4 < a.V);
+  const bool gput = ILV ? (lane & 6) == 0 && (FULL || gidx * 16 < a.V)
+                        : (t & (LPG - 1)) == 0 && (FULL || t * 4 < a.V);
   volatile uint32_t* abortp = &abort_flag;
   bool ok = true;  // every wait of this thread completed
   // code rows on 32- (16-) byte boundaries take one 32-byte store a thread
@@ -386,7 +430,53 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
           st_stream_if(vok[k2], norow + voff[k2], v[k2]);
       }
     }
-    if constexpr (QM == kQGroup) {
+    if constexpr (QM == kQGroup && ILV) {
+      // Two 1x128 groups an octet: slots 0-1 belong to group A, slots 2-3 to
+      // group B. Both maxima travel in one bf16 pair (A low, B high) through
+      // the octet's three butterfly steps.
+      const uint32_t pa = absmax_bf2(vec_absmax(v[0]), vec_absmax(v[1]));
+      const uint32_t pb = absmax_bf2(vec_absmax(v[2]), vec_absmax(v[3]));
+      // (the sign bits of absmax results are meaningless: combine magnitudes
+      // once more, then clear them before any plain max)
+      uint32_t p =
+          absmax_bf2(__byte_perm(pa, pb, 0x5410), __byte_perm(pa, pb, 0x7632)) & 0x7fff7fffu;
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) p = max_bf2(p, __shfl_xor_sync(0xffffffffu, p, o));
+      const float2 am = bf2_to_f2(p);
+      const float sa = make_scale(am.x, kPow2), sb = make_scale(am.y, kPow2);
+      float ra, rb;
+      if constexpr (kPow2) {  // exact reciprocals of powers of two: negate the exponent
+        ra = __uint_as_float((254u << 23) - __float_as_uint(sa));
+        rb = __uint_as_float((254u << 23) - __float_as_uint(sb));
+      } else {
+        ra = __frcp_rn(sa);
+        rb = __frcp_rn(sb);
+      }
+      // lanes 0 and 1 of the octet write the scales of groups A and B
+      put_group_scale<SK>(gput, a, row, srow, goff, gidx, (lane & 1) ? sb : sa);
+      if constexpr (SK == kSkE8Swz)
+        if (a.n_groups_pad > a.n_groups) zero_scale_padding(a, row, a.n_groups, t, T);
+      uint32_t* qthr = reinterpret_cast<uint32_t*>(qrow + (int64_t)tvec * 8);
+#pragma unroll
+      for (int k2 = 0; k2 < NV; ++k2) {
+        const float rcs = k2 < 2 ? ra : rb, ns = k2 < 2 ? -sa : -sb;
+        const float2 rc2 = make_float2(rcs, rcs), nb = make_float2(ns, ns);
+        float2 y[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          if constexpr (kPow2)
+            y[j] = __fmul2_rn(bf2_to_f2(v[k2][j]), rc2);  // n * 2^-e is exact
+          else
+            y[j] = div2_rn(bf2_to_f2(v[k2][j]), nb, rc2);
+        }
+        // 8 codes of vector tvec + 8 k2: an octet writes 64 contiguous bytes
+        if constexpr (FULL)
+          st_stream2(qthr + 16 * k2, f4_to_e4m3x4(y[0], y[1]), f4_to_e4m3x4(y[2], y[3]));
+        else
+          st_stream2_if(vok[k2], qthr + 16 * k2, f4_to_e4m3x4(y[0], y[1]),
+                        f4_to_e4m3x4(y[2], y[3]));
+      }
+    } else if constexpr (QM == kQGroup) {
       // chunk maximum, combined over the LPG lanes of the group
       uint32_t p = absmax_bf2(absmax_bf2(vec_absmax(v[0]), vec_absmax(v[1])),
                               absmax_bf2(vec_absmax(v[2]), vec_absmax(v[3]))) &
