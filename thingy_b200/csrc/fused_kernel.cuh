@@ -363,6 +363,22 @@ __device__ __forceinline__ float make_scale(float amax, bool pow2) {
   return s;
 }
 
+// RN(1 / s) for a scale that make_scale produced without the power-of-two
+// rounding, by Markstein's reciprocal iteration (P. Markstein, IBM J. Res.
+// Dev. 34(1), 1990): y0 = rcp.approx(s), at most 1 ulp from 1/s (PTX ISA);
+// e = RN(1 - s*y0); y1 = RN(y0 + e*y0). One step is not correctly rounded for
+// every fp32 s, but it is for every scale this path can produce, s =
+// max(RN(a / 448), 1e-4) with a a bf16 magnitude (16969 values), from any
+// start within 2 ulps of 1/s: tests/test_scale_reciprocal.py checks all of
+// them in exact rational arithmetic. Three instructions instead of the
+// general correctly rounded reciprocal.
+__device__ __forceinline__ float rcp_scale(float s) {
+  float y;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(s));
+  const float e = __fmaf_rn(-s, y, 1.0f);
+  return __fmaf_rn(e, y, y);
+}
+
 // Byte offset of scale (row, g) in the Blackwell block-scaled GEMM layout:
 // 128x4 tiles of 512 bytes, row-block major; inside a tile row r sits at
 // (r%32)*16 + (r/32)*4 and group column c at +c.
@@ -718,7 +734,7 @@ __global__ void __launch_bounds__(NCH == 1 ? 1024 : 512) fused_rmsnorm_fp8_kerne
         for (int c = 0; c < NCH; ++c) {
           sc[c] = make_scale(m[c], pow2);
           // a power-of-two scale has an exact reciprocal: negate the exponent
-          rc[c] = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(sc[c])) : __frcp_rn(sc[c]);
+          rc[c] = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(sc[c])) : rcp_scale(sc[c]);
           const int ch = c * T + t;  // chunk index in the row
           if ((t & (LPG - 1)) == 0 && (c == 0 ? chunk_ok0 : (FULL || ch * 4 < a.V)))
             put_scale(a, row, srow, ch / LPG, sc[c]);
@@ -738,7 +754,7 @@ __global__ void __launch_bounds__(NCH == 1 ? 1024 : 512) fused_rmsnorm_fp8_kerne
           flip ^= 1;
         }
         const float s1 = make_scale(m, pow2);
-        const float r1 = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(s1)) : __frcp_rn(s1);
+        const float r1 = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(s1)) : rcp_scale(s1);
 #pragma unroll
         for (int c = 0; c < NCH; ++c) {
           sc[c] = s1;
@@ -1029,7 +1045,7 @@ __global__ void __launch_bounds__(kRowwarpWarps * 32, RES ? 6 : 8)
 #pragma unroll
         for (int o = LPG / 2; o > 0; o >>= 1) p = max_bf2(p, __shfl_xor_sync(0xffffffffu, p, o));
         const float sc = make_scale(__uint_as_float(p << 16), pow2);
-        const float rc = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(sc)) : __frcp_rn(sc);
+        const float rc = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(sc)) : rcp_scale(sc);
         const int c = pc * 32 + lane;
         if ((lane & (LPG - 1)) == 0 && (FULL || c * 4 < V)) put_scale(a, row, srow, c / LPG, sc);
         store_codes(pc, sc, rc);
@@ -1046,7 +1062,7 @@ __global__ void __launch_bounds__(kRowwarpWarps * 32, RES ? 6 : 8)
       }
       const float m = warp_reduce<true>(fmaxf(__uint_as_float(pm << 16), __uint_as_float(pm & 0xffff0000u)));
       const float sc = make_scale(m, pow2);
-      const float rc = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(sc)) : __frcp_rn(sc);
+      const float rc = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(sc)) : rcp_scale(sc);
       if (lane == 0) store_scale(a, row, 0, sc);
       // ---- pass 3: codes (normalised values recomputed: same bits)
       for (int pc = 0; pc < np; ++pc) {

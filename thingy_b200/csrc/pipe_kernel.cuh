@@ -19,10 +19,10 @@
 //  * the "finisher" of row k, warp k % nw, waits for all partial sums of row
 //    k (published one iteration earlier), turns them into inv_rms and
 //    publishes it through a second 4-deep mbarrier ring;
-//  * phase B: wait for row k's inv_rms, read the row from its stage again,
-//    count this warp out of the stage (a shared-memory counter; the last
-//    warp out refills the stage with row k + S), then normalise, take group
-//    maxima, write scales and FP8 codes.
+//  * phase B: read the row from its stage again (and the weights), count
+//    this warp out of the stage (a shared-memory counter; the last warp out
+//    refills the stage with row k + S), wait for row k's inv_rms, then
+//    normalise, take group maxima, write scales and FP8 codes.
 //
 // A warp can run up to about three rows ahead of the slowest one, which is
 // why the rings are four deep (the argument is spelled out at the rings).
@@ -193,8 +193,8 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
     pipe_rmsnorm_fp8_kernel(const FusedArgs a) {
   static_assert(QM == kQGroup || QM == kQNone, "group or no quantization");
   static_assert(QM != kQGroup || LPG == 1 || LPG == 2 || LPG == 4, "lanes per group");
-  constexpr int NV = 4;  // 4 vectors (32 elements) a thread
   constexpr bool ILV = PipeLayout<QM, LPG>::kInterleaved;
+  constexpr int NV = 4;  // 4 vectors (32 elements) a thread
   constexpr bool kPow2 = SK != kSkF32;
   constexpr int kEsz = (SK == kSkE8 || SK == kSkE8Swz) ? 1 : 4;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -292,8 +292,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   // interleaved: lanes 0 and 1 of each octet, for its two groups)
   const int gidx = ILV ? warp * 8 + (lane >> 3) * 2 + (lane & 1) : t / LPG;
   const int64_t goff = (int64_t)gidx * a.s_grp * kEsz;
-  const bool gput = ILV ? (lane & 6) == 0 && (FULL || gidx * 16 < a.V)
-                        : (t & (LPG - 1)) == 0 && (FULL || t * 4 < a.V);
+  const bool gput = ILV ? (lane & 6) == 0 : (t & (LPG - 1)) == 0 && (FULL || t * 4 < a.V);
   volatile uint32_t* abortp = &abort_flag;
   bool ok = true;  // every wait of this thread completed
   // code rows on 32- (16-) byte boundaries take one 32-byte store a thread
@@ -381,8 +380,9 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
                      uint8_t* norow) {
     const int slot = k & (kPipeRing - 1);
     const uint32_t par = (uint32_t)(k >> 2) & 1u;
-    ok &= mbar_wait_abortable(smem_addr(&inv_bar[slot]), par, abortp);
-    const float inv = inv_slot[slot];
+    // The row has been in this stage since phase A and the weights never
+    // change: both are read, and the stage released, before the wait for
+    // inv_rms, so their latency overlaps it and the refill starts earlier.
     const uint32_t base = ring + (uint32_t)s * stage_bytes;
     uint32_t v[NV][4];
 #pragma unroll
@@ -415,100 +415,105 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
       w[k2][2] = u.z;
       w[k2][3] = u.w;
     }
+    ok &= mbar_wait_abortable(smem_addr(&inv_bar[slot]), par, abortp);
+    const float inv = inv_slot[slot];
     const float2 inv2 = make_float2(inv, inv);
+    {
 #pragma unroll
-    for (int k2 = 0; k2 < NV; ++k2)
+      for (int k2 = 0; k2 < 4; ++k2)
 #pragma unroll
-      for (int j = 0; j < 4; ++j)
-        v[k2][j] = mul_bf2(f2_to_bf2(__fmul2_rn(bf2_to_f2(v[k2][j]), inv2)), w[k2][j]);
-    if (store_no) {
+        for (int j = 0; j < 4; ++j)
+          v[k2][j] = mul_bf2(f2_to_bf2(__fmul2_rn(bf2_to_f2(v[k2][j]), inv2)), w[k2][j]);
+      if (store_no) {
 #pragma unroll
-      for (int k2 = 0; k2 < NV; ++k2) {
-        if constexpr (FULL)
-          st_stream(norow + voff[k2], v[k2]);
-        else
-          st_stream_if(vok[k2], norow + voff[k2], v[k2]);
-      }
-    }
-    if constexpr (QM == kQGroup && ILV) {
-      // Two 1x128 groups an octet: slots 0-1 belong to group A, slots 2-3 to
-      // group B. Both maxima travel in one bf16 pair (A low, B high) through
-      // the octet's three butterfly steps.
-      const uint32_t pa = absmax_bf2(vec_absmax(v[0]), vec_absmax(v[1]));
-      const uint32_t pb = absmax_bf2(vec_absmax(v[2]), vec_absmax(v[3]));
-      // (the sign bits of absmax results are meaningless: combine magnitudes
-      // once more, then clear them before any plain max)
-      uint32_t p =
-          absmax_bf2(__byte_perm(pa, pb, 0x5410), __byte_perm(pa, pb, 0x7632)) & 0x7fff7fffu;
-#pragma unroll
-      for (int o = 1; o < 8; o <<= 1) p = max_bf2(p, __shfl_xor_sync(0xffffffffu, p, o));
-      const float2 am = bf2_to_f2(p);
-      const float sa = make_scale(am.x, kPow2), sb = make_scale(am.y, kPow2);
-      float ra, rb;
-      if constexpr (kPow2) {  // exact reciprocals of powers of two: negate the exponent
-        ra = __uint_as_float((254u << 23) - __float_as_uint(sa));
-        rb = __uint_as_float((254u << 23) - __float_as_uint(sb));
-      } else {
-        ra = __frcp_rn(sa);
-        rb = __frcp_rn(sb);
-      }
-      // lanes 0 and 1 of the octet write the scales of groups A and B
-      put_group_scale<SK>(gput, a, row, srow, goff, gidx, (lane & 1) ? sb : sa);
-      if constexpr (SK == kSkE8Swz)
-        if (a.n_groups_pad > a.n_groups) zero_scale_padding(a, row, a.n_groups, t, T);
-      uint32_t* qthr = reinterpret_cast<uint32_t*>(qrow + (int64_t)tvec * 8);
-#pragma unroll
-      for (int k2 = 0; k2 < NV; ++k2) {
-        const float rcs = k2 < 2 ? ra : rb, ns = k2 < 2 ? -sa : -sb;
-        const float2 rc2 = make_float2(rcs, rcs), nb = make_float2(ns, ns);
-        float2 y[4];
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if constexpr (kPow2)
-            y[j] = __fmul2_rn(bf2_to_f2(v[k2][j]), rc2);  // n * 2^-e is exact
+        for (int k2 = 0; k2 < 4; ++k2) {
+          if constexpr (FULL)
+            st_stream(norow + voff[k2], v[k2]);
           else
-            y[j] = div2_rn(bf2_to_f2(v[k2][j]), nb, rc2);
+            st_stream_if(vok[k2], norow + voff[k2], v[k2]);
         }
-        // 8 codes of vector tvec + 8 k2: an octet writes 64 contiguous bytes
-        if constexpr (FULL)
-          st_stream2(qthr + 16 * k2, f4_to_e4m3x4(y[0], y[1]), f4_to_e4m3x4(y[2], y[3]));
-        else
-          st_stream2_if(vok[k2], qthr + 16 * k2, f4_to_e4m3x4(y[0], y[1]),
-                        f4_to_e4m3x4(y[2], y[3]));
       }
-    } else if constexpr (QM == kQGroup) {
-      // chunk maximum, combined over the LPG lanes of the group
-      uint32_t p = absmax_bf2(absmax_bf2(vec_absmax(v[0]), vec_absmax(v[1])),
-                              absmax_bf2(vec_absmax(v[2]), vec_absmax(v[3]))) &
-                   0x7fff7fffu;
-      p = max_bf2(p, p >> 16);
+      if constexpr (QM == kQGroup && ILV) {
+        // Two 1x128 groups an octet: slots 0-1 belong to group A, slots 2-3
+        // to group B. Both maxima travel in one bf16 pair
+        // (A low, B high) through the octet's three butterfly steps.
+        const uint32_t pa = absmax_bf2(vec_absmax(v[0]), vec_absmax(v[1]));
+        const uint32_t pb = absmax_bf2(vec_absmax(v[2]), vec_absmax(v[3]));
+        // (the sign bits of absmax results are meaningless: combine magnitudes
+        // once more, then clear them before any plain max)
+        uint32_t p =
+            absmax_bf2(__byte_perm(pa, pb, 0x5410), __byte_perm(pa, pb, 0x7632)) & 0x7fff7fffu;
 #pragma unroll
-      for (int o = LPG / 2; o > 0; o >>= 1) p = max_bf2(p, __shfl_xor_sync(0xffffffffu, p, o));
-      const float sc = make_scale(__uint_as_float(p << 16), kPow2);
-      // a power-of-two scale has an exact reciprocal: negate the exponent
-      const float rc = kPow2 ? __uint_as_float((254u << 23) - __float_as_uint(sc)) : __frcp_rn(sc);
-      put_group_scale<SK>(gput, a, row, srow, goff, gidx, sc);
-      if constexpr (SK == kSkE8Swz)
-        if (a.n_groups_pad > a.n_groups) zero_scale_padding(a, row, a.n_groups, t, T);
-      const float2 rc2 = make_float2(rc, rc), nb = make_float2(-sc, -sc);
-      uint32_t cw[NV][2];
+        for (int o = 1; o < 8; o <<= 1) p = max_bf2(p, __shfl_xor_sync(0xffffffffu, p, o));
+        const float2 am = bf2_to_f2(p);
+        const float sa = make_scale(am.x, kPow2), sb = make_scale(am.y, kPow2);
+        float ra, rb;
+        if constexpr (kPow2) {  // exact reciprocals of powers of two: negate the exponent
+          ra = __uint_as_float((254u << 23) - __float_as_uint(sa));
+          rb = __uint_as_float((254u << 23) - __float_as_uint(sb));
+        } else {
+          ra = rcp_scale(sa);
+          rb = rcp_scale(sb);
+        }
+        // lanes 0 and 1 of the octet write the scales of groups A and B
+        put_group_scale<SK>(gput && (FULL || gidx * 16 < a.V), a, row, srow, goff, gidx,
+                            (lane & 1) ? sb : sa);
+        if constexpr (SK == kSkE8Swz)
+          if (a.n_groups_pad > a.n_groups) zero_scale_padding(a, row, a.n_groups, t, T);
+        uint32_t* qthr = reinterpret_cast<uint32_t*>(qrow + (int64_t)tvec * 8);
 #pragma unroll
-      for (int k2 = 0; k2 < NV; ++k2) {
-        float2 y[4];
+        for (int k2 = 0; k2 < 4; ++k2) {
+          const float rcs = k2 < 2 ? ra : rb, ns = k2 < 2 ? -sa : -sb;
+          const float2 rc2 = make_float2(rcs, rcs), nb = make_float2(ns, ns);
+          float2 y[4];
 #pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          if constexpr (kPow2)
-            y[j] = __fmul2_rn(bf2_to_f2(v[k2][j]), rc2);  // n * 2^-e is exact
+          for (int j = 0; j < 4; ++j) {
+            if constexpr (kPow2)
+              y[j] = __fmul2_rn(bf2_to_f2(v[k2][j]), rc2);  // n * 2^-e is exact
+            else
+              y[j] = div2_rn(bf2_to_f2(v[k2][j]), nb, rc2);
+          }
+          // 8 codes of vector tvec + 8 k2: an octet writes 64 contiguous bytes
+          if constexpr (FULL)
+            st_stream2(qthr + 16 * k2, f4_to_e4m3x4(y[0], y[1]), f4_to_e4m3x4(y[2], y[3]));
           else
-            y[j] = div2_rn(bf2_to_f2(v[k2][j]), nb, rc2);
+            st_stream2_if(vok[k2], qthr + 16 * k2, f4_to_e4m3x4(y[0], y[1]),
+                          f4_to_e4m3x4(y[2], y[3]));
         }
-        cw[k2][0] = f4_to_e4m3x4(y[0], y[1]);
-        cw[k2][1] = f4_to_e4m3x4(y[2], y[3]);
+      } else if constexpr (QM == kQGroup) {
+        // chunk maximum, combined over the LPG lanes of the group
+        uint32_t p = absmax_bf2(absmax_bf2(vec_absmax(v[0]), vec_absmax(v[1])),
+                                absmax_bf2(vec_absmax(v[2]), vec_absmax(v[3]))) &
+                     0x7fff7fffu;
+        p = max_bf2(p, p >> 16);
+#pragma unroll
+        for (int o = LPG / 2; o > 0; o >>= 1) p = max_bf2(p, __shfl_xor_sync(0xffffffffu, p, o));
+        const float sc = make_scale(__uint_as_float(p << 16), kPow2);
+        // a power-of-two scale has an exact reciprocal: negate the exponent
+        const float rc = kPow2 ? __uint_as_float((254u << 23) - __float_as_uint(sc)) : rcp_scale(sc);
+        put_group_scale<SK>(gput, a, row, srow, goff, gidx, sc);
+        if constexpr (SK == kSkE8Swz)
+          if (a.n_groups_pad > a.n_groups) zero_scale_padding(a, row, a.n_groups, t, T);
+        const float2 rc2 = make_float2(rc, rc), nb = make_float2(-sc, -sc);
+        uint32_t cw[4][2];
+#pragma unroll
+        for (int k2 = 0; k2 < 4; ++k2) {
+          float2 y[4];
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if constexpr (kPow2)
+              y[j] = __fmul2_rn(bf2_to_f2(v[k2][j]), rc2);  // n * 2^-e is exact
+            else
+              y[j] = div2_rn(bf2_to_f2(v[k2][j]), nb, rc2);
+          }
+          cw[k2][0] = f4_to_e4m3x4(y[0], y[1]);
+          cw[k2][1] = f4_to_e4m3x4(y[2], y[3]);
+        }
+        // back to vector order, whole 32-byte sectors where the rows allow
+        uint32_t d[8];
+        unrotate_chunk(cw, 0, rot, d);
+        store_chunk_codes<FULL>(qrow + 32 * t, d, q32, q16, 4 * t, a.V);
       }
-      // back to vector order, whole 32-byte sectors where the rows allow
-      uint32_t d[8];
-      unrotate_chunk(cw, 0, rot, d);
-      store_chunk_codes<FULL>(qrow + 32 * t, d, q32, q16, 4 * t, a.V);
     }
   };
 
