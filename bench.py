@@ -49,6 +49,8 @@ def _kernel_name(w, threads_per_row) -> str:
     """The kernel that carries the timed step (the launch shape rules of csrc/capi.cu)."""
     if w.kind == "rms_f32":
         return "rmsnorm_f32_kernel"
+    if w.kind == "bwd":
+        return "rmsnorm_backward_kernel"
     if threads_per_row == 32:
         return "rowwarp_rmsnorm_fp8_kernel"
     if w.group_size is None:  # per-token scaling: the single-pass kernel
@@ -208,6 +210,21 @@ class Workspace:
             self.out = torch.empty_like(self.x)
             self.res = None
             return
+        if w.kind == "bwd":
+            from thingy_b200.ops import backward_workspace_bytes
+
+            self.dn = src["d_normalized"].clone()
+            self.r = src["r"].clone()
+            self.dro = src["d_residual_out"].clone() if "d_residual_out" in src else None
+            self.dx = torch.empty_like(self.r)
+            self.dw = torch.empty(w.H, dtype=torch.bfloat16, device=device)
+            self.ws = torch.empty(backward_workspace_bytes(M, w.H, device), dtype=torch.uint8,
+                                  device=device)
+            self.q = (torch.empty(M, w.H, dtype=torch.float8_e4m3fn, device=device)
+                      if w.group_size else None)
+            self.scale = (tb.empty_scale(M, w.H, 128, w.scale_format, w.scale_layout, device)
+                          if w.group_size else None)
+            return
         self.x = src["x"].clone()
         self.res = src["residual"].clone() if "residual" in src else None
         self.q = torch.empty(M, w.H, dtype=torch.float8_e4m3fn, device=device)
@@ -239,10 +256,18 @@ def run_ours(args, rank, world, local_rank):
 
     from thingy_b200.ops import launch_rms_norm
 
+    from thingy_b200.ops import launch_rms_norm_backward
+
     def step(i):  # one launch on the current stream
         s = ws[i % n_ws]
         if w.kind == "rms_f32":
             launch_rms_norm(s.x, weight, w.eps, s.out, threads_per_row=args.threads_per_row)
+            return
+        if w.kind == "bwd":  # backward: two kernels (rows, then the d_weight reduction)
+            launch_rms_norm_backward(
+                s.dn, s.r, weight, w.eps, dx=s.dx, d_residual_out=s.dro, d_weight=s.dw,
+                workspace=s.ws, q=s.q, scale=s.scale, scale_format=w.scale_format,
+                scale_layout=w.scale_layout)
             return
         launch_rms_norm_fp8(
             s.x, weight, w.eps, residual=s.res, q=s.q, scale=s.scale, residual_out=s.res_out,
@@ -378,7 +403,8 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": scaling,
         "vs_baseline": None,
-        "dtype": "bf16 in, fp32 statistics, e4m3 out",
+        "dtype": ("bf16 gradients, fp32 sums, e4m3 dx" if w.kind == "bwd"
+                  else "bf16 in, fp32 statistics, e4m3 out"),
         "data": "synthetic (seeded; shapes and distributions of the workload)",
         "config": {
             "workload": w.name,
@@ -412,7 +438,7 @@ def run_ours(args, rank, world, local_rank):
         },
         "cpu_baseline": cpu,
         "e2e": e2e,
-        "gpu_launches": K,
+        "gpu_launches": K * (2 if w.kind == "bwd" else 1),
         "clocks": clocks.summary(window) if clocks else None,
     }
     if rank == 0:
@@ -511,7 +537,8 @@ def run_reference(args, rank, world):
         "higher_is_better": True,
         "scaling": "weak",
         "vs_baseline": None,
-        "dtype": "bf16 in, fp32 statistics, e4m3 out",
+        "dtype": ("bf16 gradients, fp32 sums, e4m3 dx" if w.kind == "bwd"
+                  else "bf16 in, fp32 statistics, e4m3 out"),
         "data": "synthetic (seeded; shapes and distributions of the workload)",
         "config": {"workload": w.name, "rows_per_step": rows, "H": w.H,
                    "group_size": w.group_size or "per-token", "scale_format": w.scale_format,

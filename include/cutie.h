@@ -32,6 +32,7 @@
 #ifndef CUTIE_H_
 #define CUTIE_H_
 
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -144,6 +145,40 @@ CUTIE_API int cutie_per_token_cast_to_fp8(const void* x, int64_t ldx,
 CUTIE_API int cutie_rms_norm(const void* x, int64_t ldx, const void* weight, float eps,
                    int64_t M, int64_t H, int dtype,
                    void* out, int64_t ldo, int threads_per_row, void* stream);
+
+/*
+ * Backward of cutie_rms_norm_fp8 (bf16, with or without a residual). The
+ * reference has no backward pass (src/cutie/rms_norm/bench.py is forward
+ * only); these are the gradients torch autograd gives its PyTorch forward
+ * (bench.py:58-65 and the residual add of bench.py:97), op for op in fp32:
+ *   inv = the forward's inv_rms of r;  dt = bf16(dn * w);  b = sum(dt * r)
+ *   dx  = bf16(bf16(dt * inv + ((-0.5 * b) * inv^3 / H) * (2 * r)) + dro)
+ *   dw  = bf16(sum over rows of bf16(dn * bf16(r * inv)))
+ * d_normalized (dn): bf16 [M, H] gradient of the normalized output;
+ * r: bf16 [M, H], the forward's RMSNorm input (x + residual, i.e.
+ * residual_out, or x); d_residual_out (dro): gradient of residual_out, or
+ * NULL; dx: bf16 [M, H], the gradient of x and of residual; d_weight: bf16
+ * [H] or NULL. The weight gradient is summed per CTA into `workspace` (fp32,
+ * at least cutie_rms_norm_backward_workspace(M, H) bytes, 16-byte aligned,
+ * caller-owned, contents need not be initialised) and reduced over CTAs in a
+ * fixed order, so it is deterministic. quant_mode CUTIE_QUANT_GROUP with
+ * group_size 128 also writes dx as FP8 codes q + scales (formats and layouts
+ * as in cutie_rms_norm_fp8); CUTIE_QUANT_NONE writes none. H % 8 == 0,
+ * H <= 32768. Asynchronous on `stream`; nothing is allocated.
+ */
+CUTIE_API int cutie_rms_norm_backward(const void* d_normalized, int64_t ldd,
+                                      const void* r, int64_t ldr, const void* weight,
+                                      const void* d_residual_out, int64_t lddr,
+                                      float eps, int64_t M, int64_t H,
+                                      void* dx, int64_t lddx, void* d_weight,
+                                      void* workspace, size_t workspace_bytes,
+                                      int quant_mode, int group_size, int scale_fmt,
+                                      int scale_layout, int64_t ld_scale,
+                                      void* q, int64_t ldq, void* scale, void* stream);
+
+/* Workspace bytes cutie_rms_norm_backward needs for d_weight on the current
+ * device (one fp32 row of H partial sums per CTA of its grid). */
+CUTIE_API size_t cutie_rms_norm_backward_workspace(int64_t M, int64_t H);
 
 /*
  * Device-side status of this library's kernels on the current device: 0 when

@@ -12,6 +12,8 @@ It restates the reference's own PyTorch path with the same torch CPU ops:
                          other=0.0 :45-49, amax :50, clamp :51, UE8M0 :52-53,
                          divide :54, e4m3 cast :57)
   fp32 rms_norm          src/cutie/rms_norm/rms_norm.py:11-20 (eager form)
+  backward               torch autograd of the forward above (the reference
+                         has no backward pass)
 generalised to one scale per row (group = H), 1x32 / 1x64 groups and e8m0
 bytes, which the reference does not implement (its quantizer asserts
 gran_k == 128, fp8_utils.py:67).
@@ -121,6 +123,81 @@ def rms_norm_fp8(
     n = rms_norm_reference(r, weight, eps)
     q, s = quantize(n, group_size, scale_format)
     return q, s, (r if residual is not None else None), n
+
+
+class _IeeeRsqrt(torch.autograd.Function):
+    """RN(1 / RN(sqrt(v))) with a correctly rounded square root, and rsqrt's
+    autograd rule (-0.5 * grad * result^3).
+
+    Eager torch on some CPUs (AVX-512 builds) returns a float32 sqrt 1 ulp off
+    for some inputs; the reference computes on the GPU, whose sqrt is IEEE.
+    The float64 sqrt rounded to float32, and the float64 quotient rounded to
+    float32, are the correctly rounded float32 results (double rounding is
+    innocuous for sqrt and division at these precisions).
+    """
+
+    @staticmethod
+    def forward(ctx, v):
+        root = torch.sqrt(v.double()).float()
+        y = (1.0 / root.double()).float()
+        ctx.save_for_backward(y)
+        return y
+
+    @staticmethod
+    def backward(ctx, grad):
+        (y,) = ctx.saved_tensors
+        return -0.5 * grad * y.pow(3)
+
+
+def rms_norm_fp8_backward(
+    x: torch.Tensor,
+    weight: torch.Tensor,
+    d_normalized: torch.Tensor,
+    eps: float = 1e-6,
+    residual: torch.Tensor | None = None,
+    d_residual_out: torch.Tensor | None = None,
+    group_size: int | None = None,
+    scale_format: str = "fp32",
+    ieee_rsqrt: bool = True,
+):
+    """Gradients of rms_norm_fp8's differentiable outputs, by torch autograd.
+
+    The reference has no backward pass; its forward (bench.py:58-65 and the
+    residual add of bench.py:97, restated above with the same torch ops) is
+    differentiated by autograd on the CPU. The FP8 codes and scales are not
+    differentiable: the gradient that reaches them arrives as
+    ``d_normalized`` (the bf16 gradient of the normalized output), and
+    ``d_residual_out`` is the gradient of residual_out (the residual stream).
+
+    Returns (dx, d_weight, q, scale): dx is the gradient of x (and of
+    residual, which receives the same tensor); q / scale quantize dx like
+    ``quantize`` (None when scale_format is None). ieee_rsqrt (default)
+    takes inv_rms with an IEEE square root (see _IeeeRsqrt); False is the
+    literal eager rms_norm_reference.
+    """
+    xg = x.detach().clone().requires_grad_(True)
+    wg = weight.detach().clone().requires_grad_(True)
+    if residual is not None:
+        rg = residual.detach().clone().requires_grad_(True)
+        r = residual_add(xg, rg)
+    else:
+        r = xg
+    if ieee_rsqrt:  # rms_norm_reference's ops with the IEEE rsqrt of the GPU
+        r_f32 = r.float()
+        inv = _IeeeRsqrt.apply(r_f32.square().mean(dim=-1, keepdim=True) + eps)
+        n = (r_f32 * inv).to(r.dtype) * wg
+    else:
+        n = rms_norm_reference(r, wg, eps)
+    outs, grads = [n], [d_normalized]
+    if residual is not None and d_residual_out is not None:
+        outs.append(r)
+        grads.append(d_residual_out)
+    torch.autograd.backward(outs, grads)
+    dx = xg.grad
+    q = s = None
+    if scale_format is not None:
+        q, s = quantize(dx, group_size, scale_format)
+    return dx, wg.grad, q, s
 
 
 def mx_swizzle(scales: np.ndarray) -> np.ndarray:

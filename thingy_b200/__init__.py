@@ -9,11 +9,15 @@ Drop-in host API for the reference's hot path (S1ro1/thingy, package
     per_token_cast_to_fp8(_triton)          <- src/cutie/vendor/prime_rl/fp8_utils.py:63-89
     rms_norm_fp8                            general form (per-token / 1xG / MXFP8,
                                                fp32 / pow2 / e8m0 scales, layouts)
+    rms_norm_fp8_backward, ResidualRMSNormFP8
+                                            backward (no counterpart in the reference):
+                                               the gradients autograd gives its forward
 
 Every op runs hand-written CUDA from ``lib/libcutie_b200.so`` through the C
 ABI in ``include/cutie.h``; there is no CPU or PyTorch fallback.
 """
 
+from .backward import ResidualRMSNormFP8, rms_norm_fp8_backward
 from .fp8_utils import per_token_cast_to_fp8, per_token_cast_to_fp8_triton
 from .fused import empty_scale, residual_rms_norm_fp8, rms_norm_fp8
 from .layouts import mx_swizzle, mx_swizzle_offset, mx_swizzled_size, mx_unswizzle
@@ -21,6 +25,7 @@ from .rms_norm import RMSNorm, rms_norm, rms_norm_on_stream
 
 __all__ = [
     "RMSNorm",
+    "ResidualRMSNormFP8",
     "empty_scale",
     "mx_swizzle",
     "mx_swizzle_offset",
@@ -31,5 +36,6 @@ __all__ = [
     "residual_rms_norm_fp8",
     "rms_norm",
     "rms_norm_fp8",
+    "rms_norm_fp8_backward",
     "rms_norm_on_stream",
 ]

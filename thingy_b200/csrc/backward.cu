@@ -1,0 +1,308 @@
+// Backward of the fused [residual add] -> RMSNorm path, with optional FP8
+// quantization of the input gradient, for sm_100a.
+//
+// The reference has no backward pass. What is computed is what torch
+// autograd computes for the reference's forward (src/cutie/rms_norm/bench.py:
+// 58-65 and the residual add of :97), op for op in fp32. Per row, with r the
+// RMSNorm input (x + residual), dn the gradient of the bf16 normalized output
+// and dro the gradient of residual_out:
+//
+//   inv  = RN(1 / RN(sqrt(RN(sum r^2) / H + eps)))     (the forward's value)
+//   dt   = bf16(dn * w)                                  (bf16 mul backward)
+//   b    = sum dt * r                                    (fp32)
+//   dvar = (-0.5 * b) * ((inv * inv) * inv)              (rsqrt backward)
+//   dsq  = dvar / H                                      (mean backward)
+//   dx   = bf16(dt * inv + dsq * (2 * r))                (mul + square backward)
+//   dr   = bf16(dx + dro)                                (gradient accumulation)
+//   dw  += bf16(dn * bf16(r * inv))  over rows           (fp32 sums)
+//
+// dr is the gradient of x and of residual. Both row sums (sum r^2 and
+// sum dt * r) take one block reduction of a float pair. The weight gradient
+// is summed per CTA in shared memory, written as one fp32 row of partial
+// sums per CTA to a caller-provided workspace, and reduced over CTAs in a
+// fixed order by a second kernel, so it is deterministic.
+//
+// Thread layout: the interleaved layout of the pipelined forward kernel (lane
+// i of octet o of warp w holds vectors w*128 + o*32 + i + 8k), read directly
+// from global memory: an octet reads 128 contiguous bytes per slot, and an
+// octet covers two whole 1x128 groups, so the optional quantization of dr is
+// the forward's two-groups-an-octet scheme.
+#include "launch.cuh"
+
+namespace cutie {
+
+__device__ __forceinline__ void st_bf16x8(void* p, const uint32_t (&v)[4], bool ok) {
+  st_stream_if(ok, p, v);
+}
+
+// MAXT: the largest block of the instantiation; 256 leaves 128 registers a
+// thread (rows of up to 8192), 1024 caps them at 64 (wider rows spill).
+template <bool RES, bool QUANT, bool DW, bool FULL, int MAXT>
+__global__ void __launch_bounds__(MAXT, MAXT <= 256 ? 2 : 1)
+    rmsnorm_backward_kernel(const BwdArgs a, float eps, float rcp_H) {
+  constexpr int NV = 4;
+  extern __shared__ __align__(16) float wacc[];  // [V * 8] partial dw of this CTA
+  __shared__ float2 red[2][32];
+
+  const FusedArgs& qa = a.qa;
+  const int T = blockDim.x;
+  const int t = threadIdx.x, lane = t & 31, warp = t >> 5, nw = T >> 5;
+  const int V = qa.V;
+  const int tvec = warp * 128 + (lane >> 3) * 32 + (lane & 7);
+  bool vok[NV];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) vok[k] = FULL || tvec + 8 * k < V;
+
+  if (DW)
+    for (int i = t; i < V * 8; i += T) wacc[i] = 0.0f;
+  // weights: the same columns for every row
+  griddep_wait();  // inputs of the previous kernel are complete from here on
+  uint32_t w[NV][4];
+#pragma unroll
+  for (int k = 0; k < NV; ++k) {
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (vok[k]) u = ld_keep(a.w + (int64_t)(tvec + 8 * k) * 8);
+    w[k][0] = u.x;
+    w[k][1] = u.y;
+    w[k][2] = u.z;
+    w[k][3] = u.w;
+  }
+  griddep_launch_dependents();
+  __syncthreads();
+
+  // this thread's quantization group and whether it writes its scale (lanes
+  // 0 and 1 of an octet, for the octet's two groups)
+  const int gidx = warp * 8 + (lane >> 3) * 2 + (lane & 1);
+  const bool gput = (lane & 6) == 0 && (FULL || gidx * 16 < V);
+  const int64_t goff = (int64_t)gidx * qa.s_grp * ((qa.scale_fmt == kFmtE8M0) ? 1 : 4);
+  int flip = 0;
+
+  for (int64_t row = blockIdx.x; row < qa.M; row += gridDim.x) {
+    const uint16_t* rrow = a.r + row * a.ldr;
+    const uint16_t* drow = a.dn + row * a.lddn;
+    uint32_t rv[NV][4], dv[NV][4];
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      uint4 u = make_uint4(0u, 0u, 0u, 0u), e = make_uint4(0u, 0u, 0u, 0u);
+      if (vok[k]) {
+        u = ld_stream(rrow + (int64_t)(tvec + 8 * k) * 8);
+        e = ld_stream(drow + (int64_t)(tvec + 8 * k) * 8);
+      }
+      rv[k][0] = u.x; rv[k][1] = u.y; rv[k][2] = u.z; rv[k][3] = u.w;
+      dv[k][0] = e.x; dv[k][1] = e.y; dv[k][2] = e.z; dv[k][3] = e.w;
+    }
+    // (sum r^2, sum dt * r): squares per pair in the forward's order, then
+    // the products; one butterfly on the pair of sums
+    float2 sq = make_float2(0.0f, 0.0f), pr = make_float2(0.0f, 0.0f);
+#pragma unroll
+    for (int k = 0; k < NV; ++k)
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 rf = bf2_to_f2(rv[k][j]);
+        const float2 dt = bf2_to_f2(mul_bf2(dv[k][j], w[k][j]));
+        sq = __ffma2_rn(rf, rf, sq);
+        pr = __ffma2_rn(dt, rf, pr);
+      }
+    float2 s2 = make_float2(__fadd_rn(sq.x, sq.y), __fadd_rn(pr.x, pr.y));
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      s2.x = __fadd_rn(s2.x, __shfl_xor_sync(0xffffffffu, s2.x, o));
+      s2.y = __fadd_rn(s2.y, __shfl_xor_sync(0xffffffffu, s2.y, o));
+    }
+    if (lane == 0) red[flip][warp] = s2;
+    __syncthreads();
+    float2 tot = lane < nw ? red[flip][lane] : make_float2(0.0f, 0.0f);
+    flip ^= 1;
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      tot.x = __fadd_rn(tot.x, __shfl_xor_sync(0xffffffffu, tot.x, o));
+      tot.y = __fadd_rn(tot.y, __shfl_xor_sync(0xffffffffu, tot.y, o));
+    }
+    float mean = div_rn(tot.x, (float)qa.H, rcp_H);
+    if (mean < 0x1p-100f) mean = __fdiv_rn(tot.x, (float)qa.H);
+    const float inv = __frcp_rn(__fsqrt_rn(__fadd_rn(mean, eps)));
+    const float dvar = __fmul_rn(__fmul_rn(-0.5f, tot.y), __fmul_rn(__fmul_rn(inv, inv), inv));
+    const float dsq = __fdiv_rn(dvar, (float)qa.H);
+    const float2 inv2 = make_float2(inv, inv), dsq2 = make_float2(dsq, dsq);
+
+    uint16_t* xrow = a.dx + row * a.lddx;
+    const uint16_t* grow = RES ? a.dro + row * a.lddro : nullptr;
+#pragma unroll
+    for (int k = 0; k < NV; ++k) {
+      uint4 g = make_uint4(0u, 0u, 0u, 0u);
+      if (RES && vok[k]) g = ld_stream(grow + (int64_t)(tvec + 8 * k) * 8);
+      const uint32_t gg[4] = {g.x, g.y, g.z, g.w};
+      float* acc = wacc + (tvec + 8 * k) * 8;
+      float4 a0 = make_float4(0.f, 0.f, 0.f, 0.f), a1 = a0;
+      if (DW && vok[k]) {
+        a0 = *reinterpret_cast<float4*>(acc);
+        a1 = *reinterpret_cast<float4*>(acc + 4);
+      }
+      float2 accp[4] = {make_float2(a0.x, a0.y), make_float2(a0.z, a0.w),
+                        make_float2(a1.x, a1.y), make_float2(a1.z, a1.w)};
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const float2 rf = bf2_to_f2(rv[k][j]);
+        const float2 dt = bf2_to_f2(mul_bf2(dv[k][j], w[k][j]));
+        // dt * inv + dsq * (2 r), each product rounded, then the sum
+        // dt * inv + dsq * (2 r): both products rounded, then the sum. The
+        // sum is taken with the scalar __fadd_rn, which is never merged into
+        // a multiply-add (packed fp32x2 multiplies and adds were, even as
+        // explicit .rn instructions: the result came out rounded once).
+        const float2 g1 = __fmul2_rn(dt, inv2);
+        const float2 g2 = __fmul2_rn(dsq2, __fadd2_rn(rf, rf));
+        uint32_t d = f2_to_bf2(make_float2(__fadd_rn(g1.x, g2.x), __fadd_rn(g1.y, g2.y)));
+        if (RES) d = add_bf2(d, gg[j]);
+        if (DW) {
+          const uint32_t tb = f2_to_bf2(__fmul2_rn(rf, inv2));  // the forward's bf16(r * inv)
+          accp[j] = __fadd2_rn(accp[j], bf2_to_f2(mul_bf2(dv[k][j], tb)));
+        }
+        rv[k][j] = d;  // rv now holds dr
+      }
+      if (DW && vok[k]) {
+        *reinterpret_cast<float4*>(acc) = make_float4(accp[0].x, accp[0].y, accp[1].x, accp[1].y);
+        *reinterpret_cast<float4*>(acc + 4) =
+            make_float4(accp[2].x, accp[2].y, accp[3].x, accp[3].y);
+      }
+      st_bf16x8(xrow + (int64_t)(tvec + 8 * k) * 8, rv[k], vok[k]);
+    }
+
+    if constexpr (QUANT) {
+      // two 1x128 groups an octet (slots 0-1, 2-3), as in the forward kernel
+      const uint32_t pa = absmax_bf2(vec_absmax(rv[0]), vec_absmax(rv[1]));
+      const uint32_t pb = absmax_bf2(vec_absmax(rv[2]), vec_absmax(rv[3]));
+      uint32_t p =
+          absmax_bf2(__byte_perm(pa, pb, 0x5410), __byte_perm(pa, pb, 0x7632)) & 0x7fff7fffu;
+#pragma unroll
+      for (int o = 1; o < 8; o <<= 1) p = max_bf2(p, __shfl_xor_sync(0xffffffffu, p, o));
+      const float2 am = bf2_to_f2(p);
+      const bool pow2 = qa.scale_fmt != kFmtF32;
+      const float sa = make_scale(am.x, pow2), sb = make_scale(am.y, pow2);
+      const float ra = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(sa)) : rcp_scale(sa);
+      const float rb = pow2 ? __uint_as_float((254u << 23) - __float_as_uint(sb)) : rcp_scale(sb);
+      char* srow = static_cast<char*>(qa.scale) +
+                   row * qa.s_row * ((qa.scale_fmt == kFmtE8M0) ? 1 : 4);
+      if (gput) {
+        if (qa.scale_layout == kLaySwizzled)
+          put_scale(qa, row, srow, gidx, (lane & 1) ? sb : sa);
+        else if (qa.scale_fmt == kFmtE8M0)
+          srow[goff] = (char)(__float_as_uint((lane & 1) ? sb : sa) >> 23);
+        else
+          *reinterpret_cast<float*>(srow + goff) = (lane & 1) ? sb : sa;
+      }
+      if (qa.scale_layout == kLaySwizzled && qa.n_groups_pad > qa.n_groups)
+        zero_scale_padding(qa, row, qa.n_groups, t, T);
+      uint32_t* qthr = reinterpret_cast<uint32_t*>(qa.q + row * qa.ldq + (int64_t)tvec * 8);
+#pragma unroll
+      for (int k = 0; k < NV; ++k) {
+        const float rcs = k < 2 ? ra : rb, ns = k < 2 ? -sa : -sb;
+        const float2 rc2 = make_float2(rcs, rcs), nb = make_float2(ns, ns);
+        float2 y[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j)
+          y[j] = pow2 ? __fmul2_rn(bf2_to_f2(rv[k][j]), rc2) : div2_rn(bf2_to_f2(rv[k][j]), nb, rc2);
+        st_stream2_if(vok[k], qthr + 16 * k, f4_to_e4m3x4(y[0], y[1]), f4_to_e4m3x4(y[2], y[3]));
+      }
+    }
+  }
+  if constexpr (QUANT)  // swizzled-layout padding rows: scales only
+    if (qa.scale_layout == kLaySwizzled) {
+      const int64_t nrows = (int64_t)blockIdx.x < qa.M ? (qa.M - 1 - blockIdx.x) / gridDim.x + 1 : 0;
+      for (int64_t r = blockIdx.x + nrows * gridDim.x; r < qa.M_pad; r += gridDim.x)
+        zero_scale_padding(qa, r, 0, t, T);
+    }
+  if (DW) {
+    __syncthreads();
+    float* out = a.partial + (int64_t)blockIdx.x * V * 8;
+    for (int i = t; i < V * 8; i += T) out[i] = wacc[i];
+  }
+}
+
+// dw[j] = bf16(sum over the CTAs' partial rows, in CTA order)
+__global__ void __launch_bounds__(256) rmsnorm_backward_dw_kernel(const float* partial, int rows,
+                                                                 int H, uint16_t* dw) {
+  griddep_wait();
+  griddep_launch_dependents();
+  const int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= H) return;
+  float s = 0.0f;
+  for (int b = 0; b < rows; ++b) s = __fadd_rn(s, partial[(int64_t)b * H + j]);
+  const __nv_bfloat16 v = __float2bfloat16_rn(s);
+  dw[j] = *reinterpret_cast<const uint16_t*>(&v);
+}
+
+namespace {
+
+template <bool RES, bool QUANT, bool DW, bool FULL, int MAXT>
+cudaError_t launch_bwd_one(const BwdArgs& a, float eps, int threads, int grid, size_t smem,
+                           cudaStream_t st) {
+  auto k = rmsnorm_backward_kernel<RES, QUANT, DW, FULL, MAXT>;
+  if (smem > 48 * 1024) {
+    const cudaError_t e =
+        cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return e;
+  }
+  return launch_pdl(k, (unsigned)grid, (unsigned)threads, smem, st, a, eps,
+                    1.0f / (float)a.qa.H);
+}
+
+template <bool RES, bool QUANT, bool DW>
+cudaError_t launch_bwd3(const BwdArgs& a, float eps, int threads, int grid, size_t smem,
+                        cudaStream_t st) {
+  const bool full = (int64_t)threads * 4 == a.qa.V;
+  if (threads <= 256)
+    return full ? launch_bwd_one<RES, QUANT, DW, true, 256>(a, eps, threads, grid, smem, st)
+                : launch_bwd_one<RES, QUANT, DW, false, 256>(a, eps, threads, grid, smem, st);
+  return full ? launch_bwd_one<RES, QUANT, DW, true, 1024>(a, eps, threads, grid, smem, st)
+              : launch_bwd_one<RES, QUANT, DW, false, 1024>(a, eps, threads, grid, smem, st);
+}
+
+}  // namespace
+
+// Threads of one row and CTAs of the grid for a backward launch; the grid is
+// also the number of partial dw rows the workspace must hold.
+void backward_shape(int64_t M, int64_t H, int* threads, int* grid) {
+  const int64_t V = H / 8;
+  int T = (int)((V + 127) / 128 * 32);
+  if (T < 32) T = 32;
+  *threads = T;
+  int per_sm = 1024 / T;  // up to 1024 threads and 8 CTAs an SM
+  if (per_sm < 1) per_sm = 1;
+  if (per_sm > 8) per_sm = 8;
+  int64_t g = (int64_t)per_sm * device_sm_count();
+  if (g > M) g = M;
+  if (g < 1) g = 1;
+  *grid = (int)g;
+}
+
+cudaError_t launch_backward(const BwdArgs& a, float eps, bool dw_wanted, uint16_t* dw,
+                            int max_grid, cudaStream_t st) {
+  int T = 0, grid = 0;
+  backward_shape(a.qa.M, a.qa.H, &T, &grid);
+  if (max_grid > 0 && grid > max_grid) grid = max_grid;
+  if (a.qa.M_pad == 0)  // no rows: d_weight is zero (a sum over no partial rows)
+    return dw_wanted ? launch_pdl(rmsnorm_backward_dw_kernel, (unsigned)((a.qa.H + 255) / 256),
+                                  256u, 0, st, (const float*)a.partial, 0, a.qa.H, dw)
+                     : cudaSuccess;
+  if (a.qa.M == 0) grid = (int)(a.qa.M_pad < grid ? a.qa.M_pad : grid);
+  const size_t smem = dw_wanted ? (size_t)a.qa.V * 8 * sizeof(float) : 0;
+  const bool res = a.dro != nullptr, quant = a.qa.q != nullptr;
+  cudaError_t e;
+  if (dw_wanted) {
+    e = res ? (quant ? launch_bwd3<true, true, true>(a, eps, T, grid, smem, st)
+                     : launch_bwd3<true, false, true>(a, eps, T, grid, smem, st))
+            : (quant ? launch_bwd3<false, true, true>(a, eps, T, grid, smem, st)
+                     : launch_bwd3<false, false, true>(a, eps, T, grid, smem, st));
+  } else {
+    e = res ? (quant ? launch_bwd3<true, true, false>(a, eps, T, grid, smem, st)
+                     : launch_bwd3<true, false, false>(a, eps, T, grid, smem, st))
+            : (quant ? launch_bwd3<false, true, false>(a, eps, T, grid, smem, st)
+                     : launch_bwd3<false, false, false>(a, eps, T, grid, smem, st));
+  }
+  if (e != cudaSuccess || !dw_wanted) return e;
+  const int H = a.qa.H;
+  return launch_pdl(rmsnorm_backward_dw_kernel, (unsigned)((H + 255) / 256), 256u, 0, st,
+                    (const float*)a.partial, grid, H, dw);
+}
+
+}  // namespace cutie

@@ -494,6 +494,149 @@ extern "C" int cutie_rms_norm(const void* x, int64_t ldx, const void* weight, fl
   return CUTIE_OK;
 }
 
+extern "C" size_t cutie_rms_norm_backward_workspace(int64_t M, int64_t H) {
+  if (M < 0 || H <= 0) return 0;
+  int T = 0, grid = 0;
+  backward_shape(M, H, &T, &grid);
+  return (size_t)grid * (size_t)H * sizeof(float);
+}
+
+namespace cutie {
+namespace {
+
+// Checks the backward's arguments and fills `a`; returns CUTIE_OK, or the
+// status of the first bad argument (the workspace is checked by the caller).
+int prepare_backward(const void* d_normalized, int64_t ldd, const void* r, int64_t ldr,
+                     const void* weight, const void* d_residual_out, int64_t lddr, float eps,
+                     int64_t M, int64_t H, void* dx, int64_t lddx, void* d_weight,
+                     int quant_mode, int group_size, int scale_fmt, int scale_layout,
+                     int64_t ld_scale, void* q, int64_t ldq, void* scale, BwdArgs* a) {
+  if (M < 0 || H <= 0)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "need M >= 0 and H > 0 (got M=%lld, H=%lld)",
+                (long long)M, (long long)H);
+  if (H % 8 != 0)
+    return fail(CUTIE_ERR_UNSUPPORTED, "H=%lld must be a multiple of 8 (16-byte rows)",
+                (long long)H);
+  if (H > 32768)
+    return fail(CUTIE_ERR_UNSUPPORTED, "the backward kernel holds rows of up to 32768 (H=%lld)",
+                (long long)H);
+  if (!(eps >= 0.0f) || std::isinf(eps))
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "eps must be finite and >= 0");
+  if (quant_mode != CUTIE_QUANT_NONE &&
+      !(quant_mode == CUTIE_QUANT_GROUP && group_size == 128))
+    return fail(CUTIE_ERR_UNSUPPORTED,
+                "the backward quantizes its gradient in 1x128 groups only (quant_mode %d, "
+                "group_size %d)",
+                quant_mode, group_size);
+  if (scale_fmt < CUTIE_SCALE_FP32 || scale_fmt > CUTIE_SCALE_E8M0)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown scale_fmt %d", scale_fmt);
+  if (scale_layout < CUTIE_LAYOUT_ROW_MAJOR || scale_layout > CUTIE_LAYOUT_MX_SWIZZLED)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown scale_layout %d", scale_layout);
+  const bool quant = quant_mode != CUTIE_QUANT_NONE;
+  if (quant && scale_layout == CUTIE_LAYOUT_MX_SWIZZLED && scale_fmt != CUTIE_SCALE_E8M0)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "the swizzled scale layout needs E8M0 scales");
+  const int64_t n_groups = quant ? (H + 127) / 128 : 0;
+  const bool swz = quant && scale_layout == CUTIE_LAYOUT_MX_SWIZZLED;
+  const int64_t n_groups_pad = swz ? (n_groups + 3) / 4 * 4 : n_groups;
+  const int64_t M_pad = swz ? (M + 127) / 128 * 128 : M;
+
+  int rc;
+  if (M > 0) {
+    if ((rc = check_matrix("d_normalized", d_normalized, ldd, H, 16, 8)) != CUTIE_OK) return rc;
+    if ((rc = check_matrix("r", r, ldr, H, 16, 8)) != CUTIE_OK) return rc;
+    if ((rc = check_matrix("dx", dx, lddx, H, 16, 8)) != CUTIE_OK) return rc;
+    if (d_residual_out != nullptr &&
+        (rc = check_matrix("d_residual_out", d_residual_out, lddr, H, 16, 8)) != CUTIE_OK)
+      return rc;
+  }
+  if (weight == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "weight is NULL");
+  if (!aligned(weight, 16)) return fail(CUTIE_ERR_ALIGNMENT, "weight must be 16-byte aligned");
+  if (d_weight != nullptr && !aligned(d_weight, 2))
+    return fail(CUTIE_ERR_ALIGNMENT, "d_weight must be 2-byte aligned");
+  int64_t s_row = 0, s_grp = 0;
+  if (quant && M > 0) {
+    if ((rc = check_matrix("q", q, ldq, H, 8, 8)) != CUTIE_OK) return rc;
+    if (scale == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "scale is NULL");
+    if (scale_fmt != CUTIE_SCALE_E8M0 && !aligned(scale, 4))
+      return fail(CUTIE_ERR_ALIGNMENT, "fp32 scales must be 4-byte aligned");
+  }
+  if (quant) {
+    if (scale_layout == CUTIE_LAYOUT_ROW_MAJOR) {
+      const int64_t ld = ld_scale == 0 ? n_groups : ld_scale;
+      if (ld < n_groups)
+        return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < %lld groups",
+                    (long long)ld_scale, (long long)n_groups);
+      s_row = ld;
+      s_grp = 1;
+    } else if (scale_layout == CUTIE_LAYOUT_COL_MAJOR) {
+      const int64_t ld = ld_scale == 0 ? M : ld_scale;
+      if (ld < M)
+        return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < M=%lld", (long long)ld_scale,
+                    (long long)M);
+      s_row = 1;
+      s_grp = ld;
+    }
+  }
+  *a = BwdArgs{};
+  a->dn = static_cast<const uint16_t*>(d_normalized);
+  a->lddn = ldd;
+  a->r = static_cast<const uint16_t*>(r);
+  a->ldr = ldr;
+  a->w = static_cast<const uint16_t*>(weight);
+  a->dro = static_cast<const uint16_t*>(d_residual_out);
+  a->lddro = lddr;
+  a->dx = static_cast<uint16_t*>(dx);
+  a->lddx = lddx;
+  FusedArgs& qa = a->qa;
+  qa.q = quant ? static_cast<uint8_t*>(q) : nullptr;
+  qa.ldq = ldq;
+  qa.scale = scale;
+  qa.s_row = s_row;
+  qa.s_grp = s_grp;
+  qa.M = M;
+  qa.M_pad = M_pad;
+  qa.H = (int)H;
+  qa.V = (int)(H / 8);
+  qa.n_groups = (int)n_groups;
+  qa.n_groups_pad = (int)n_groups_pad;
+  qa.scale_fmt = scale_fmt;
+  qa.scale_layout = swz ? kLaySwizzled : kLayStrided;
+  return CUTIE_OK;
+}
+
+}  // namespace
+}  // namespace cutie
+
+extern "C" int cutie_rms_norm_backward(const void* d_normalized, int64_t ldd, const void* r,
+                                       int64_t ldr, const void* weight,
+                                       const void* d_residual_out, int64_t lddr, float eps,
+                                       int64_t M, int64_t H, void* dx, int64_t lddx,
+                                       void* d_weight, void* workspace, size_t workspace_bytes,
+                                       int quant_mode, int group_size, int scale_fmt,
+                                       int scale_layout, int64_t ld_scale, void* q, int64_t ldq,
+                                       void* scale, void* stream) {
+  g_err[0] = '\0';
+  BwdArgs a{};
+  int rc = prepare_backward(d_normalized, ldd, r, ldr, weight, d_residual_out, lddr, eps, M, H,
+                            dx, lddx, d_weight, quant_mode, group_size, scale_fmt, scale_layout,
+                            ld_scale, q, ldq, scale, &a);
+  if (rc != CUTIE_OK) return rc;
+  const bool want_dw = d_weight != nullptr;
+  if (a.qa.M_pad == 0 && !want_dw) return CUTIE_OK;
+  if (want_dw) {
+    const size_t need = cutie_rms_norm_backward_workspace(M, H);
+    if (workspace == nullptr || workspace_bytes < need || !aligned(workspace, 16))
+      return fail(CUTIE_ERR_INVALID_ARGUMENT,
+                  "d_weight needs a 16-byte aligned workspace of %zu bytes (got %zu at %p)", need,
+                  workspace_bytes, workspace);
+    a.partial = static_cast<float*>(workspace);
+  }
+  const cudaError_t e = launch_backward(a, eps, want_dw, static_cast<uint16_t*>(d_weight), 0,
+                                        static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm backward launch");
+  return CUTIE_OK;
+}
+
 extern "C" int cutie_device_error(int clear) {
   g_err[0] = '\0';
   int any = 0;

@@ -193,6 +193,29 @@ CUTIE_DECLARE_MODE(g32)
 CUTIE_DECLARE_MODE(g64)
 CUTIE_DECLARE_MODE(g128)
 
+// Backward of the fused path (backward.cu).
+struct BwdArgs {
+  const uint16_t* dn;   // d normalized, bf16 [M, H]
+  int64_t lddn;
+  const uint16_t* r;    // forward RMSNorm input (x + residual), bf16 [M, H]
+  int64_t ldr;
+  const uint16_t* w;    // weight [H]
+  const uint16_t* dro;  // d residual_out (may be null)
+  int64_t lddro;
+  uint16_t* dx;         // d x (= d residual), bf16 [M, H]
+  int64_t lddx;
+  float* partial;       // [gridDim.x, H] fp32 partial sums of dw (null: no dw)
+  FusedArgs qa;         // quantization of dx: q, ldq, scale, s_row, s_grp, n_groups(_pad),
+                        // scale_fmt, scale_layout, M, M_pad, H, V (q == null: none)
+};
+
+// Threads of a row and CTAs of a backward launch (the CTAs are also the rows
+// of dw partial sums the workspace holds).
+void backward_shape(int64_t M, int64_t H, int* threads, int* grid);
+// max_grid > 0 caps the CTAs (and so the rows of partial sums in a.partial).
+cudaError_t launch_backward(const BwdArgs& a, float eps, bool dw_wanted, uint16_t* dw,
+                            int max_grid, cudaStream_t st);
+
 struct F32Args {
   const float* x;
   int64_t ldx;

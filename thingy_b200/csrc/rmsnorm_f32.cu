@@ -40,13 +40,18 @@ __global__ void __launch_bounds__(NV > 4 ? 512 : 1024) rmsnorm_f32_kernel(const 
       v[k] = make_float4(__uint_as_float(u.x), __uint_as_float(u.y), __uint_as_float(u.z),
                          __uint_as_float(u.w));
     }
-    // x.pow(2) is rounded before the sum: multiply and add separately.
+    // x.pow(2) is rounded before the sum: multiply and add separately. The
+    // adds are the scalar __fadd_rn, which is never merged into a multiply-add
+    // (the packed fp32x2 forms are: a product feeding a packed add came out
+    // rounded once).
     float2 acc = make_float2(0.0f, 0.0f);
 #pragma unroll
     for (int k = 0; k < NV; ++k) {
       const float2 lo = make_float2(v[k].x, v[k].y), hi = make_float2(v[k].z, v[k].w);
-      acc = __fadd2_rn(acc, __fmul2_rn(lo, lo));
-      acc = __fadd2_rn(acc, __fmul2_rn(hi, hi));
+      float2 sq = __fmul2_rn(lo, lo);
+      acc = make_float2(__fadd_rn(acc.x, sq.x), __fadd_rn(acc.y, sq.y));
+      sq = __fmul2_rn(hi, hi);
+      acc = make_float2(__fadd_rn(acc.x, sq.x), __fadd_rn(acc.y, sq.y));
     }
     const float ss = block_reduce<false>(__fadd_rn(acc.x, acc.y), red[flip], lane, warp, nw);
     flip ^= 1;

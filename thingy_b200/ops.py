@@ -238,3 +238,81 @@ def launch_rms_norm(
             int(threads_per_row), _stream_handle(device, stream),
         )
     _lib.check(status)
+
+
+def backward_workspace_bytes(M: int, H: int, device=None) -> int:
+    """Bytes of fp32 workspace the backward needs for the weight gradient on ``device``."""
+    lib = _lib.load()
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        return int(lib.cutie_rms_norm_backward_workspace(int(M), int(H)))
+
+
+def launch_rms_norm_backward(
+    d_normalized: torch.Tensor,
+    r: torch.Tensor,
+    weight: torch.Tensor,
+    eps: float,
+    *,
+    dx: torch.Tensor,
+    d_residual_out: torch.Tensor | None = None,
+    d_weight: torch.Tensor | None = None,
+    workspace: torch.Tensor | None = None,
+    q: torch.Tensor | None = None,
+    scale: torch.Tensor | None = None,
+    scale_format: str = "fp32",
+    scale_layout: str = "row",
+    stream=None,
+) -> None:
+    """Enqueue the backward of [residual add] -> RMSNorm (cutie_rms_norm_backward).
+
+    d_normalized: bf16 [M, H] gradient of the normalized output; r: the
+    forward's RMSNorm input (x + residual, i.e. residual_out, or x);
+    d_residual_out: gradient of residual_out, or None. Writes dx (the
+    gradient of x and of residual), d_weight (bf16 [H], needs ``workspace``,
+    a CUDA tensor of at least backward_workspace_bytes(M, H) bytes) and, with
+    q and scale, the 1x128 FP8 quantization of dx.
+    """
+    if scale_format not in SCALE_FORMATS:
+        raise ValueError(f"scale_format must be one of {SCALE_FORMATS}")
+    if scale_layout not in SCALE_LAYOUTS:
+        raise ValueError(f"scale_layout must be one of {SCALE_LAYOUTS}")
+    M, H = _check_x(d_normalized)
+    device = d_normalized.device
+    ldd = _rows("d_normalized", d_normalized, M, H, torch.bfloat16, device)
+    ldr = _rows("r", r, M, H, torch.bfloat16, device)
+    lddx = _rows("dx", dx, M, H, torch.bfloat16, device)
+    lddr = (_rows("d_residual_out", d_residual_out, M, H, torch.bfloat16, device)
+            if d_residual_out is not None else 0)
+    if weight.shape != (H,) or weight.dtype != torch.bfloat16 or weight.device != device:
+        raise ValueError(f"weight must be a bf16 [{H}] tensor on {device}")
+    if not weight.is_contiguous():
+        raise ValueError("weight must be contiguous")
+    ws_bytes = 0
+    if d_weight is not None:
+        if d_weight.shape != (H,) or d_weight.dtype != torch.bfloat16 or d_weight.device != device:
+            raise ValueError(f"d_weight must be a bf16 [{H}] tensor on {device}")
+        if not d_weight.is_contiguous():
+            raise ValueError("d_weight must be contiguous")
+        if workspace is None or workspace.device != device or not workspace.is_contiguous():
+            raise ValueError("d_weight needs a contiguous CUDA workspace tensor")
+        ws_bytes = workspace.numel() * workspace.element_size()
+    quant = q is not None or scale is not None
+    if quant:
+        if q is None or scale is None:
+            raise ValueError("q and scale must be given together")
+        if q.dtype not in (FP8_DTYPE, torch.uint8):
+            raise ValueError(f"q must be float8_e4m3fn, got {q.dtype}")
+        ldq = _rows("q", q, M, H, q.dtype, device)
+        ld_scale = _scale_args(scale, M, H, 128, scale_format, scale_layout, device)
+        mode = _lib.QUANT_GROUP
+    else:
+        ldq, ld_scale, mode = 0, 0, _lib.QUANT_NONE
+    lib = _lib.load()
+    with torch.cuda.device(device):
+        status = lib.cutie_rms_norm_backward(
+            _ptr(d_normalized), ldd, _ptr(r), ldr, _ptr(weight), _ptr(d_residual_out), lddr,
+            float(eps), M, H, _ptr(dx), lddx, _ptr(d_weight), _ptr(workspace), ws_bytes,
+            mode, 128, _FMT_CODE[scale_format], _LAYOUT_CODE[scale_layout], ld_scale,
+            _ptr(q), ldq, _ptr(scale), _stream_handle(device, stream),
+        )
+    _lib.check(status)

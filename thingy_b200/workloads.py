@@ -44,7 +44,8 @@ class Workload:
     scale_layout: str
     residual: bool
     dist: str  # "normal", "outliers", "student_t"
-    kind: str = "fused"  # "fused" (bf16 -> fp8) or "rms_f32" (standalone fp32 RMSNorm)
+    kind: str = "fused"  # "fused" (bf16 -> fp8), "rms_f32" (standalone fp32 RMSNorm)
+    #                      or "bwd" (backward: gradients of the fused path)
 
     def bytes_moved(self, M: int | None = None) -> int:
         """Algorithmic HBM bytes of one pass: inputs read once, outputs written once.
@@ -59,6 +60,16 @@ class Workload:
         H = self.H
         if self.kind == "rms_f32":  # utils.py:10-19: x and out fp32, weight once
             return 2 * M * H * 4 + H * 4
+        if self.kind == "bwd":
+            # read d_normalized, r [, d_residual_out], weight; write dx, d_weight
+            # [, FP8 codes + scales of dx]. The per-CTA partial sums of d_weight
+            # in the workspace are not counted (not an input or output).
+            total = 2 * M * H + 2 * M * H + 2 * H + 2 * M * H + 2 * H
+            if self.residual:
+                total += 2 * M * H
+            if self.group_size:
+                total += M * H + (1 if self.scale_format == "e8m0" else 4) * M * -(-H // 128)
+            return total
         groups = 1 if not self.group_size else -(-H // self.group_size)
         scale_bytes = 1 if self.scale_format == "e8m0" else 4
         total = 2 * M * H + 2 * H + M * H + scale_bytes * M * groups
@@ -77,6 +88,8 @@ WORKLOADS = {
         Workload("mx32_decode_5120", 128, 5120, 1e-6, 32, "e8m0", "mx", False, "student_t"),
         Workload("g128_sharded_262144x8192", 262144, 8192, 1e-6, 128, "fp32", "col", False,
                  "outliers"),
+        Workload("bwd_residual_g128_16384x7168", 16384, 7168, 1e-6, 128, "fp32", "col", True,
+                 "normal", kind="bwd"),
         *(
             Workload(f"rmsnorm_f32_{m}x{h}", m, h, 1e-5, None, "fp32", "row", False, "normal",
                      kind="rms_f32")
@@ -114,6 +127,18 @@ def make_inputs(w: Workload, M: int | None = None, *, device="cpu", seed: int = 
     H = w.H
     gen = torch.Generator(device=device)
     gen.manual_seed(seed)
+    if w.kind == "bwd":  # r (= residual_out of the forward), gradients ~N(0,1)
+        weight = _weight(H, gen, device)
+        if row_offset:
+            gen.manual_seed(seed * 1_000_003 + row_offset)
+        r = (torch.randn((M, H), generator=gen, device=device)
+             + 2.0 * torch.randn((M, H), generator=gen, device=device)).to(torch.bfloat16)
+        out = {"r": r, "weight": weight, "eps": w.eps,
+               "d_normalized": torch.randn((M, H), generator=gen, device=device).to(torch.bfloat16)}
+        if w.residual:
+            out["d_residual_out"] = torch.randn((M, H), generator=gen, device=device).to(
+                torch.bfloat16)
+        return out
     if w.kind == "rms_f32":  # utils.py:38-59: randn x and weight, fp32
         if row_offset:
             gen.manual_seed(seed * 1_000_003 + row_offset)
