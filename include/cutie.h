@@ -181,6 +181,40 @@ CUTIE_API int cutie_rms_norm_backward(const void* d_normalized, int64_t ldd,
 CUTIE_API size_t cutie_rms_norm_backward_workspace(int64_t M, int64_t H);
 
 /*
+ * cutie_rms_norm_backward without a workspace argument: it allocates nothing
+ * and needs no device memory from the caller beyond inputs and outputs. It
+ * has no counterpart in the reference. It is for callers that cannot
+ * allocate device memory: code that runs where a cudaMalloc is not allowed
+ * or must not happen (inside an allocator's or a framework's callbacks, a
+ * plug-in whose host owns every device buffer, a memory pool that must not
+ * grow), or that cannot hold a workspace between calls.
+ *
+ * The partial sums of d_weight go to a device array of the library instead:
+ * 2^20 floats (4 MiB), present on every GPU that loads the library until the
+ * process exits. Its CTAs are capped so that their rows of H partial sums
+ * fit (2^20 / H CTAs, e.g. 146 at H = 7168), so d_weight is summed in a
+ * different grouping than cutie_rms_norm_backward's (the same bound on the
+ * error; dx, q and scale are identical). Sizes: as cutie_rms_norm_backward
+ * (H <= 32768, which always fits the array); a larger H is refused with
+ * CUTIE_ERR_UNSUPPORTED. Every row of the array that a call reads was
+ * written by that call, so nothing needs clearing between calls.
+ *
+ * The first call on a device looks up the array's device address there
+ * (once per device, with that device current); make that first call before
+ * any stream capture. All calls on a device share the one array, so calls
+ * that may run at the same time on the GPU (other streams, other host
+ * threads) race on it and give wrong d_weight: order them on one stream.
+ */
+CUTIE_API int cutie_rms_norm_backward_noalloc(const void* d_normalized, int64_t ldd,
+                                              const void* r, int64_t ldr, const void* weight,
+                                              const void* d_residual_out, int64_t lddr,
+                                              float eps, int64_t M, int64_t H,
+                                              void* dx, int64_t lddx, void* d_weight,
+                                              int quant_mode, int group_size, int scale_fmt,
+                                              int scale_layout, int64_t ld_scale,
+                                              void* q, int64_t ldq, void* scale, void* stream);
+
+/*
  * Device-side status of this library's kernels on the current device: 0 when
  * no kernel has hit a failure since the last clear; otherwise the first error
  * code recorded (1 = a bulk-copy wait ran out: a row never arrived in shared

@@ -34,6 +34,7 @@ EXPORTED_SYMBOLS = (
     "cutie_rms_norm",
     "cutie_rms_norm_backward",
     "cutie_rms_norm_backward_workspace",
+    "cutie_rms_norm_backward_noalloc",
     "cutie_device_error",
     "cutie_last_error",
     "cutie_abi_version",
@@ -64,6 +65,11 @@ _SIGNATURES = {
          _ptr, ctypes.c_size_t, _int, _int, _int, _int, _i64, _ptr, _i64, _ptr, _ptr],
     ),
     "cutie_rms_norm_backward_workspace": (ctypes.c_size_t, [_i64, _i64]),
+    "cutie_rms_norm_backward_noalloc": (
+        _int,
+        [_ptr, _i64, _ptr, _i64, _ptr, _ptr, _i64, _f32, _i64, _i64, _ptr, _i64, _ptr,
+         _int, _int, _int, _int, _i64, _ptr, _i64, _ptr, _ptr],
+    ),
     "cutie_device_error": (_int, [_int]),
     "cutie_last_error": (ctypes.c_char_p, []),
     "cutie_abi_version": (_int, []),

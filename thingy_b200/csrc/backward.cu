@@ -29,7 +29,37 @@
 // the forward's two-groups-an-octet scheme.
 #include "launch.cuh"
 
+#include <mutex>
+
 namespace cutie {
+
+// Scratch of cutie_rms_norm_backward_noalloc, the entry point for callers
+// that cannot allocate device memory (include/cutie.h says which): the
+// per-CTA partial sums of d_weight go to this file-scope array instead of a
+// caller-provided workspace. kNoAllocScratchFloats floats (4 MiB) on every GPU
+// that loads the library, held until the process exits. Host code cannot use
+// the array's name as a device address; noalloc_scratch() resolves it.
+static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
+
+// Device address of g_noalloc_scratch on the current device: looked up once
+// per device, with that device current, and cached.
+cudaError_t noalloc_scratch(float** out) {
+  static std::mutex mu;
+  static float* addr[kMaxScratchDevices] = {};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return e;
+  if (dev < 0 || dev >= kMaxScratchDevices) return cudaErrorInvalidDevice;
+  std::lock_guard<std::mutex> lock(mu);
+  if (addr[dev] == nullptr) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
+    if (e != cudaSuccess) return e;
+    addr[dev] = static_cast<float*>(p);
+  }
+  *out = addr[dev];
+  return cudaSuccess;
+}
 
 __device__ __forceinline__ void st_bf16x8(void* p, const uint32_t (&v)[4], bool ok) {
   st_stream_if(ok, p, v);

@@ -637,6 +637,41 @@ extern "C" int cutie_rms_norm_backward(const void* d_normalized, int64_t ldd, co
   return CUTIE_OK;
 }
 
+extern "C" int cutie_rms_norm_backward_noalloc(const void* d_normalized, int64_t ldd,
+                                               const void* r, int64_t ldr, const void* weight,
+                                               const void* d_residual_out, int64_t lddr,
+                                               float eps, int64_t M, int64_t H, void* dx,
+                                               int64_t lddx, void* d_weight, int quant_mode,
+                                               int group_size, int scale_fmt, int scale_layout,
+                                               int64_t ld_scale, void* q, int64_t ldq,
+                                               void* scale, void* stream) {
+  g_err[0] = '\0';
+  BwdArgs a{};
+  int rc = prepare_backward(d_normalized, ldd, r, ldr, weight, d_residual_out, lddr, eps, M, H,
+                            dx, lddx, d_weight, quant_mode, group_size, scale_fmt, scale_layout,
+                            ld_scale, q, ldq, scale, &a);
+  if (rc != CUTIE_OK) return rc;
+  const bool want_dw = d_weight != nullptr;
+  if (a.qa.M_pad == 0 && !want_dw) return CUTIE_OK;
+  int max_grid = 0;
+  if (want_dw) {
+    // each CTA writes one row of H partial sums into the scratch
+    if (H > kNoAllocScratchFloats)
+      return fail(CUTIE_ERR_UNSUPPORTED,
+                  "H=%lld exceeds the %lld-float device scratch of the allocation-free backward",
+                  (long long)H, (long long)kNoAllocScratchFloats);
+    float* scratch = nullptr;
+    const cudaError_t e = noalloc_scratch(&scratch);
+    if (e != cudaSuccess) return cuda_fail(e, "resolving the backward's device scratch");
+    a.partial = scratch;
+    max_grid = (int)(kNoAllocScratchFloats / H);
+  }
+  const cudaError_t e = launch_backward(a, eps, want_dw, static_cast<uint16_t*>(d_weight),
+                                        max_grid, static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "rmsnorm backward launch");
+  return CUTIE_OK;
+}
+
 extern "C" int cutie_device_error(int clear) {
   g_err[0] = '\0';
   int any = 0;

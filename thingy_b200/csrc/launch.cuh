@@ -212,6 +212,13 @@ struct BwdArgs {
 // Threads of a row and CTAs of a backward launch (the CTAs are also the rows
 // of dw partial sums the workspace holds).
 void backward_shape(int64_t M, int64_t H, int* threads, int* grid);
+// Floats of the d_weight scratch the allocation-free backward keeps in a
+// device array of the library (backward.cu), and that array's address on the
+// current device (resolved once per device).
+constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 20;
+constexpr int kMaxScratchDevices = 64;
+cudaError_t noalloc_scratch(float** out);
+
 // max_grid > 0 caps the CTAs (and so the rows of partial sums in a.partial).
 cudaError_t launch_backward(const BwdArgs& a, float eps, bool dw_wanted, uint16_t* dw,
                             int max_grid, cudaStream_t st);
