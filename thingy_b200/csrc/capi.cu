@@ -676,7 +676,8 @@ extern "C" int cutie_device_error(int clear) {
   g_err[0] = '\0';
   int any = 0;
   cudaError_t (*readers[])(int*, bool) = {device_error_none, device_error_token, device_error_g32,
-                                          device_error_g64, device_error_g128};
+                                          device_error_g64, device_error_g128,
+                                          device_error_bwd};
   for (auto read : readers) {
     int v = 0;
     const cudaError_t e = read(&v, clear != 0);

@@ -219,6 +219,9 @@ constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 20;
 constexpr int kMaxScratchDevices = 64;
 cudaError_t noalloc_scratch(float** out);
 
+// Device error word of backward.cu (see read_device_error).
+cudaError_t device_error_bwd(int* out, bool clear);
+
 // max_grid > 0 caps the CTAs (and so the rows of partial sums in a.partial).
 cudaError_t launch_backward(const BwdArgs& a, float eps, bool dw_wanted, uint16_t* dw,
                             int max_grid, cudaStream_t st);
