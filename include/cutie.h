@@ -80,6 +80,15 @@ enum cutie_scale_layout {
    * inside a tile (m%32)*16 + ((m%128)/32)*4 + g%4. Rows are padded to a
    * multiple of 128 and groups to a multiple of 4; padding bytes are written
    * as 0. Requires CUTIE_SCALE_E8M0. ld_scale is ignored.                   */
+  CUTIE_LAYOUT_COL_MAJOR_PACKED = 3, /* e8m0 exponents packed four to a     */
+  /* little-endian 32-bit word along the groups, words M-major: scale (m, g) is
+   * byte g%4 of word (g/4)*ld_scale + m, i.e. byte offset
+   * (g/4)*4*ld_scale + 4*m + g%4 (the packed UE8M0 scale tensor that
+   * DeepGEMM-style SM100 FP8 GEMMs take: int32 [M, ceil(G/4)], stride
+   * (1, ld_scale)). ld_scale counts words, >= M; 0 means M rounded up to a
+   * multiple of 4 (16-byte aligned columns). Bytes of groups past the last
+   * one in the final word are not written. Requires CUTIE_SCALE_E8M0.
+   * No counterpart in the reference, which writes fp32 row-major scales.  */
 };
 
 /* ---- element types for cutie_rms_norm ----------------------------------- */

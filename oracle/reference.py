@@ -200,6 +200,21 @@ def rms_norm_fp8_backward(
     return dx, wg.grad, q, s
 
 
+def ue8m0_pack(scales: np.ndarray) -> np.ndarray:
+    """[M, G] e8m0 bytes -> [ceil(G/4), ld] int32 words, ld = M rounded up to 4.
+
+    Word (j, m) holds the exponents of groups 4j..4j+3 of row m, group 4j in
+    the least significant byte; missing groups and pad rows are 0. Written
+    independently of thingy_b200.layouts (which the kernel mirrors).
+    """
+    M, G = scales.shape
+    W, ld = -(-G // 4), -(-M // 4) * 4
+    out = np.zeros((W, ld), dtype=np.int64)
+    for g in range(G):
+        out[g // 4, :M] |= scales[:, g].astype(np.int64) << (8 * (g % 4))
+    return out.astype(np.uint32).view(np.int32)
+
+
 def mx_swizzle(scales: np.ndarray) -> np.ndarray:
     """[M, G] e8m0 bytes -> flat Blackwell block-scaled layout (zero padded).
 
@@ -228,4 +243,6 @@ def layout_scales(scale: torch.Tensor, layout: str) -> np.ndarray:
         return np.ascontiguousarray(s.T)
     if layout == "mx":
         return mx_swizzle(s)
+    if layout == "packed":
+        return ue8m0_pack(s)
     raise ValueError(layout)

@@ -6,7 +6,7 @@ import numpy as np
 import torch
 
 from oracle import reference as ora
-from thingy_b200.layouts import mx_unswizzle, n_groups
+from thingy_b200.layouts import mx_unswizzle, n_groups, unpack_ue8m0
 
 
 def bf16_bits(t: torch.Tensor) -> np.ndarray:
@@ -41,6 +41,8 @@ def scale_matrix(s: torch.Tensor, M: int, H: int, group_size, fmt: str, layout: 
     """The GPU's scales as an [M, G] array (uint8 exponents for e8m0)."""
     G = n_groups(H, group_size)
     s = s.detach().cpu()
+    if layout == "packed":  # int32 [M, W] view over [W, ld] words
+        return unpack_ue8m0(s.reshape(M, -1).t().contiguous().numpy(), M, G)
     if fmt == "e8m0":
         s = s.view(torch.uint8)
     if layout == "mx":
@@ -103,6 +105,10 @@ def check_parity(inp: dict, group_size, fmt: str, layout: str, *, exact: bool = 
     if layout == "mx":  # the whole buffer, zero padding included
         np.testing.assert_array_equal(
             s.detach().cpu().view(torch.uint8).numpy(), ora.layout_scales(s_own, "mx")
+        )
+    if layout == "packed" and M > 0:  # whole words of the M rows, zero pad bytes included
+        np.testing.assert_array_equal(
+            s.detach().cpu().reshape(M, -1).t().numpy(), ora.layout_scales(s_own, "packed")[:, :M]
         )
     # end to end against the oracle
     gs = H if not group_size else group_size

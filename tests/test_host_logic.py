@@ -103,3 +103,40 @@ def test_empty_scale_shapes():
     s = tb.empty_scale(10, 5120, 32, "e8m0", "mx")
     assert s.numel() == 128 * 160 and s.element_size() == 1
     assert tb.empty_scale(10, 4096, None).shape == (10, 1)
+
+
+def test_packed_ue8m0_layout_known_answer():
+    """Four exponents a little-endian int32 word along the groups, words M-major."""
+    from oracle import reference as ora
+
+    s = np.array([[1, 2, 3, 4, 5], [6, 7, 8, 9, 10], [11, 12, 13, 14, 255]], dtype=np.uint8)
+    words = layouts.pack_ue8m0(s)
+    assert words.dtype == np.int32 and words.shape == (2, 4)  # ld = 3 rounded up to 4
+    assert words.view(np.uint32)[0].tolist() == [0x04030201, 0x09080706, 0x0E0D0C0B, 0]
+    assert words.view(np.uint32)[1].tolist() == [0x05, 0x0A, 0xFF, 0]
+    np.testing.assert_array_equal(ora.ue8m0_pack(s), words)
+    np.testing.assert_array_equal(layouts.unpack_ue8m0(words, 3, 5), s)
+    rng = np.random.default_rng(1)
+    for M, G in [(1, 1), (7, 56), (130, 7), (5, 4)]:
+        a = rng.integers(0, 256, (M, G)).astype(np.uint8)
+        np.testing.assert_array_equal(ora.ue8m0_pack(a), layouts.pack_ue8m0(a))
+        np.testing.assert_array_equal(layouts.unpack_ue8m0(layouts.pack_ue8m0(a), M, G), a)
+
+
+def test_packed_scale_allocation_and_validation():
+    from thingy_b200.ops import _scale_args
+
+    s = tb.empty_scale(10, 7168, 128, "e8m0", "packed")  # 56 groups: 14 words a row
+    assert s.shape == (10, 14) and s.stride() == (1, 12) and s.dtype == torch.int32
+    assert _scale_args(s, 10, 7168, 128, "e8m0", "packed", s.device) == 12
+    assert _scale_args(s.t(), 10, 7168, 128, "e8m0", "packed", s.device) == 12
+    z = tb.empty_scale(6, 200 * 8, 128, "e8m0", "packed")  # 13 groups: last word padded
+    assert z.shape == (6, 4) and int(z.abs().sum()) == 0
+    with pytest.raises(ValueError):
+        tb.empty_scale(10, 7168, 128, "fp32", "packed")
+    with pytest.raises(ValueError):  # packed words are int32
+        _scale_args(torch.zeros(10, 14, dtype=torch.uint8), 10, 7168, 128, "e8m0", "packed",
+                    torch.device("cpu"))
+    with pytest.raises(ValueError):  # row-contiguous is not the packed layout
+        _scale_args(torch.zeros(10, 14, dtype=torch.int32), 10, 7168, 128, "e8m0", "packed",
+                    torch.device("cpu"))

@@ -40,6 +40,8 @@ MODES = [
     (32, "e8m0", "mx"),
     (32, "e8m0", "row"),
     (32, "fp32", "col"),
+    (128, "e8m0", "packed"),
+    (32, "e8m0", "packed"),
 ]
 
 

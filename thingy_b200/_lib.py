@@ -23,7 +23,7 @@ ERR_CUDA = -4
 
 QUANT_NONE, QUANT_TOKEN, QUANT_GROUP = 0, 1, 2
 SCALE_FP32, SCALE_FP32_POW2, SCALE_E8M0 = 0, 1, 2
-LAYOUT_ROW_MAJOR, LAYOUT_COL_MAJOR, LAYOUT_MX_SWIZZLED = 0, 1, 2
+LAYOUT_ROW_MAJOR, LAYOUT_COL_MAJOR, LAYOUT_MX_SWIZZLED, LAYOUT_COL_MAJOR_PACKED = 0, 1, 2, 3
 DTYPE_BF16, DTYPE_F32 = 0, 1
 
 ABI_VERSION = 1

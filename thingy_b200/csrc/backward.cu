@@ -108,7 +108,8 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 256 ? 2 : 1)
   // 0 and 1 of an octet, for the octet's two groups)
   const int gidx = warp * 8 + (lane >> 3) * 2 + (lane & 1);
   const bool gput = (lane & 6) == 0 && (FULL || gidx * 16 < V);
-  const int64_t goff = (int64_t)gidx * qa.s_grp * ((qa.scale_fmt == kFmtE8M0) ? 1 : 4);
+  const int64_t goff = ((int64_t)(gidx >> 2) * qa.s_grp4 + (int64_t)(gidx & 3) * qa.s_grp) *
+                       ((qa.scale_fmt == kFmtE8M0) ? 1 : 4);
   int flip = 0;
 
   for (int64_t row = blockIdx.x; row < qa.M; row += gridDim.x) {
@@ -354,7 +355,8 @@ __global__ void __launch_bounds__(256, 2)
   // 0 and 1 of an octet, for the octet's two groups)
   const int gidx = warp * 8 + (lane >> 3) * 2 + (lane & 1);
   const bool gput = (lane & 6) == 0 && (FULL || gidx * 16 < V);
-  const int64_t goff = (int64_t)gidx * qa.s_grp * ((qa.scale_fmt == kFmtE8M0) ? 1 : 4);
+  const int64_t goff = ((int64_t)(gidx >> 2) * qa.s_grp4 + (int64_t)(gidx & 3) * qa.s_grp) *
+                       ((qa.scale_fmt == kFmtE8M0) ? 1 : 4);
   float2 dwa[NV][4];
 #pragma unroll
   for (int k = 0; k < NV; ++k)

@@ -301,6 +301,44 @@ int check_matrix(const char* name, const void* p, int64_t ld, int64_t H, uintptr
   return CUTIE_OK;
 }
 
+// Strides of a strided scale layout: element offset of (row m, group g) =
+// m*s_row + (g/4)*s_grp4 + (g%4)*s_grp. Row- and column-major take ld_scale
+// elements (0: dense); the packed layout takes ld_scale 32-bit words (0: M
+// rounded up to 4, 16-byte aligned columns) and e8m0 scales only.
+int strided_scale(int layout, int fmt, int64_t ld_scale, int64_t M, int64_t n_groups,
+                  int64_t* s_row, int64_t* s_grp, int64_t* s_grp4) {
+  if (layout == CUTIE_LAYOUT_ROW_MAJOR) {
+    const int64_t ld = ld_scale == 0 ? n_groups : ld_scale;
+    if (ld < n_groups)
+      return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < %lld groups",
+                  (long long)ld_scale, (long long)n_groups);
+    *s_row = ld;
+    *s_grp = 1;
+  } else if (layout == CUTIE_LAYOUT_COL_MAJOR) {
+    const int64_t ld = ld_scale == 0 ? M : ld_scale;
+    if (ld < M)
+      return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < M=%lld", (long long)ld_scale,
+                  (long long)M);
+    *s_row = 1;
+    *s_grp = ld;
+  } else if (layout == CUTIE_LAYOUT_COL_MAJOR_PACKED) {
+    if (fmt != CUTIE_SCALE_E8M0)
+      return fail(CUTIE_ERR_INVALID_ARGUMENT, "the packed scale layout needs E8M0 scales");
+    const int64_t ld = ld_scale == 0 ? (M + 3) / 4 * 4 : ld_scale;
+    if (ld < M)
+      return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld words < M=%lld",
+                  (long long)ld_scale, (long long)M);
+    *s_row = 4;  // bytes: one 32-bit word a row
+    *s_grp = 1;
+    *s_grp4 = 4 * ld;
+    return CUTIE_OK;
+  } else {
+    return CUTIE_OK;  // swizzled: addressed by its own map
+  }
+  *s_grp4 = 4 * *s_grp;
+  return CUTIE_OK;
+}
+
 int run_fused(bool norm, const void* x, int64_t ldx, const void* residual, int64_t ldr,
               const void* weight, float eps, int64_t M, int64_t H, int quant_mode,
               int group_size, int scale_fmt, int scale_layout, int64_t ld_scale, void* q,
@@ -320,7 +358,7 @@ int run_fused(bool norm, const void* x, int64_t ldx, const void* residual, int64
     return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown quant_mode %d", quant_mode);
   if (scale_fmt < CUTIE_SCALE_FP32 || scale_fmt > CUTIE_SCALE_E8M0)
     return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown scale_fmt %d", scale_fmt);
-  if (scale_layout < CUTIE_LAYOUT_ROW_MAJOR || scale_layout > CUTIE_LAYOUT_MX_SWIZZLED)
+  if (scale_layout < CUTIE_LAYOUT_ROW_MAJOR || scale_layout > CUTIE_LAYOUT_COL_MAJOR_PACKED)
     return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown scale_layout %d", scale_layout);
   const bool quant = quant_mode != CUTIE_QUANT_NONE;
   if (!norm && !quant)
@@ -357,27 +395,15 @@ int run_fused(bool norm, const void* x, int64_t ldx, const void* residual, int64
     if (weight == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "weight is NULL");
     if (!aligned(weight, 16)) return fail(CUTIE_ERR_ALIGNMENT, "weight must be 16-byte aligned");
   }
-  int64_t s_row = 0, s_grp = 0;
+  int64_t s_row = 0, s_grp = 0, s_grp4 = 0;
   if (quant) {
     if ((rc = check_matrix("q", q, ldq, H, 8, 8)) != CUTIE_OK) return rc;
     if (scale == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "scale is NULL");
     if (scale_fmt != CUTIE_SCALE_E8M0 && !aligned(scale, 4))
       return fail(CUTIE_ERR_ALIGNMENT, "fp32 scales must be 4-byte aligned");
-    if (scale_layout == CUTIE_LAYOUT_ROW_MAJOR) {
-      const int64_t ld = ld_scale == 0 ? n_groups : ld_scale;
-      if (ld < n_groups)
-        return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < %lld groups",
-                    (long long)ld_scale, (long long)n_groups);
-      s_row = ld;
-      s_grp = 1;
-    } else if (scale_layout == CUTIE_LAYOUT_COL_MAJOR) {
-      const int64_t ld = ld_scale == 0 ? M : ld_scale;
-      if (ld < M)
-        return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < M=%lld", (long long)ld_scale,
-                    (long long)M);
-      s_row = 1;
-      s_grp = ld;
-    }
+    if ((rc = strided_scale(scale_layout, scale_fmt, ld_scale, M, n_groups, &s_row, &s_grp,
+                            &s_grp4)) != CUTIE_OK)
+      return rc;
   }
 
   const int64_t V = H / 8;
@@ -402,6 +428,7 @@ int run_fused(bool norm, const void* x, int64_t ldx, const void* residual, int64
   a.scale = scale;
   a.s_row = s_row;
   a.s_grp = s_grp;
+  a.s_grp4 = s_grp4;
   a.M = M;
   a.M_pad = M_pad;
   a.H = (int)H;
@@ -530,7 +557,7 @@ int prepare_backward(const void* d_normalized, int64_t ldd, const void* r, int64
                 quant_mode, group_size);
   if (scale_fmt < CUTIE_SCALE_FP32 || scale_fmt > CUTIE_SCALE_E8M0)
     return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown scale_fmt %d", scale_fmt);
-  if (scale_layout < CUTIE_LAYOUT_ROW_MAJOR || scale_layout > CUTIE_LAYOUT_MX_SWIZZLED)
+  if (scale_layout < CUTIE_LAYOUT_ROW_MAJOR || scale_layout > CUTIE_LAYOUT_COL_MAJOR_PACKED)
     return fail(CUTIE_ERR_INVALID_ARGUMENT, "unknown scale_layout %d", scale_layout);
   const bool quant = quant_mode != CUTIE_QUANT_NONE;
   if (quant && scale_layout == CUTIE_LAYOUT_MX_SWIZZLED && scale_fmt != CUTIE_SCALE_E8M0)
@@ -553,7 +580,7 @@ int prepare_backward(const void* d_normalized, int64_t ldd, const void* r, int64
   if (!aligned(weight, 16)) return fail(CUTIE_ERR_ALIGNMENT, "weight must be 16-byte aligned");
   if (d_weight != nullptr && !aligned(d_weight, 2))
     return fail(CUTIE_ERR_ALIGNMENT, "d_weight must be 2-byte aligned");
-  int64_t s_row = 0, s_grp = 0;
+  int64_t s_row = 0, s_grp = 0, s_grp4 = 0;
   if (quant && M > 0) {
     if ((rc = check_matrix("q", q, ldq, H, 8, 8)) != CUTIE_OK) return rc;
     if (scale == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "scale is NULL");
@@ -561,21 +588,9 @@ int prepare_backward(const void* d_normalized, int64_t ldd, const void* r, int64
       return fail(CUTIE_ERR_ALIGNMENT, "fp32 scales must be 4-byte aligned");
   }
   if (quant) {
-    if (scale_layout == CUTIE_LAYOUT_ROW_MAJOR) {
-      const int64_t ld = ld_scale == 0 ? n_groups : ld_scale;
-      if (ld < n_groups)
-        return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < %lld groups",
-                    (long long)ld_scale, (long long)n_groups);
-      s_row = ld;
-      s_grp = 1;
-    } else if (scale_layout == CUTIE_LAYOUT_COL_MAJOR) {
-      const int64_t ld = ld_scale == 0 ? M : ld_scale;
-      if (ld < M)
-        return fail(CUTIE_ERR_INVALID_ARGUMENT, "ld_scale %lld < M=%lld", (long long)ld_scale,
-                    (long long)M);
-      s_row = 1;
-      s_grp = ld;
-    }
+    if ((rc = strided_scale(scale_layout, scale_fmt, ld_scale, M, n_groups, &s_row, &s_grp,
+                            &s_grp4)) != CUTIE_OK)
+      return rc;
   }
   *a = BwdArgs{};
   a->dn = static_cast<const uint16_t*>(d_normalized);
@@ -593,6 +608,7 @@ int prepare_backward(const void* d_normalized, int64_t ldd, const void* r, int64
   qa.scale = scale;
   qa.s_row = s_row;
   qa.s_grp = s_grp;
+  qa.s_grp4 = s_grp4;
   qa.M = M;
   qa.M_pad = M_pad;
   qa.H = (int)H;

@@ -59,8 +59,9 @@ struct FusedArgs {
   uint8_t* q;           // e4m3 codes
   int64_t ldq;
   void* scale;          // fp32 or e8m0 bytes
-  int64_t s_row;        // strided layout: element offset = row*s_row + g*s_grp
-  int64_t s_grp;
+  int64_t s_row;        // strided layouts: element offset of (row, g) =
+  int64_t s_grp;        //   row*s_row + (g/4)*s_grp4 + (g%4)*s_grp
+  int64_t s_grp4;       // (4*s_grp, except for e8m0 bytes packed 4 to a word)
   int64_t M;            // rows with data
   int64_t M_pad;        // rows incl. swizzle padding (== M unless swizzled)
   int H;                // columns
@@ -393,7 +394,7 @@ __device__ __forceinline__ void store_scale(const FusedArgs& a, int64_t row, int
   if (a.scale_layout == kLaySwizzled) {
     static_cast<uint8_t*>(a.scale)[swizzled_offset(row, g, a.n_groups_pad >> 2)] = e8;
   } else {
-    const int64_t off = row * a.s_row + (int64_t)g * a.s_grp;
+    const int64_t off = row * a.s_row + (int64_t)(g >> 2) * a.s_grp4 + (int64_t)(g & 3) * a.s_grp;
     if (a.scale_fmt == kFmtE8M0)
       static_cast<uint8_t*>(a.scale)[off] = e8;
     else
@@ -453,10 +454,12 @@ __device__ __forceinline__ void put_scale(const FusedArgs& a, int64_t row, char*
   if (a.scale_layout == kLaySwizzled) {
     static_cast<uint8_t*>(a.scale)[swizzled_offset(row, g, a.n_groups_pad >> 2)] =
         (uint8_t)(__float_as_uint(s) >> 23);
-  } else if (a.scale_fmt == kFmtE8M0) {
-    srow[(int64_t)g * a.s_grp] = (char)(__float_as_uint(s) >> 23);
   } else {
-    reinterpret_cast<float*>(srow)[(int64_t)g * a.s_grp] = s;
+    const int64_t off = (int64_t)(g >> 2) * a.s_grp4 + (int64_t)(g & 3) * a.s_grp;
+    if (a.scale_fmt == kFmtE8M0)
+      srow[off] = (char)(__float_as_uint(s) >> 23);
+    else
+      reinterpret_cast<float*>(srow)[off] = s;
   }
 }
 

@@ -291,7 +291,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   // whether it writes the scale (leader lane of a group inside the row;
   // interleaved: lanes 0 and 1 of each octet, for its two groups)
   const int gidx = ILV ? warp * 8 + (lane >> 3) * 2 + (lane & 1) : t / LPG;
-  const int64_t goff = (int64_t)gidx * a.s_grp * kEsz;
+  const int64_t goff = ((int64_t)(gidx >> 2) * a.s_grp4 + (int64_t)(gidx & 3) * a.s_grp) * kEsz;
   const bool gput = ILV ? (lane & 6) == 0 : (t & (LPG - 1)) == 0 && (FULL || t * 4 < a.V);
   volatile uint32_t* abortp = &abort_flag;
   bool ok = true;  // every wait of this thread completed

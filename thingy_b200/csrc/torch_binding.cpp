@@ -45,6 +45,18 @@ const void* ptr_or_null(const c10::optional<at::Tensor>& t) {
 // ld_scale for (layout, groups) from the scale tensor's shape and strides;
 // mirrors thingy_b200.ops._scale_args.
 int64_t scale_ld(const at::Tensor& s, int64_t M, int64_t G, int64_t layout) {
+  if (layout == CUTIE_LAYOUT_COL_MAJOR_PACKED) {  // int32 words, four groups a word
+    const int64_t W = (G + 3) / 4;
+    if (s.dim() == 1 && W == 1) {
+      if (s.size(0) != M || (M > 1 && s.stride(0) != 1)) bad("packed per-row scales must be a contiguous [M] tensor");
+      return M;
+    }
+    if (s.dim() != 2) bad("packed scales must be 2-D");
+    const int64_t a = s.size(0), b = s.size(1);
+    if (a == M && b == W && (M <= 1 || s.stride(0) == 1)) return W > 1 ? std::max<int64_t>(s.stride(1), M) : M;
+    if (a == W && b == M && (M <= 1 || s.stride(1) == 1)) return W > 1 ? std::max<int64_t>(s.stride(0), M) : M;
+    bad("packed scales must be an int32 [M, ceil(n_groups/4)] tensor contiguous along M (or its transpose)");
+  }
   if (layout == CUTIE_LAYOUT_MX_SWIZZLED) {
     if (!s.is_contiguous()) bad("swizzled scales need a contiguous buffer");
     const int64_t need = (M + 127) / 128 * 128 * ((G + 3) / 4 * 4);
@@ -102,7 +114,9 @@ void rms_norm_fp8(const at::Tensor& x, const c10::optional<at::Tensor>& weight, 
       bad("q must be float8_e4m3fn");
     ldq = rows_ld(*q, "q", M, H, q->scalar_type(), dev);
     const int64_t G = group_size > 0 ? (H + group_size - 1) / group_size : 1;
-    if (scale_fmt == CUTIE_SCALE_E8M0) {
+    if (scale_layout == CUTIE_LAYOUT_COL_MAJOR_PACKED) {
+      if (scale->scalar_type() != at::kInt) bad("packed e8m0 scales must be int32 words");
+    } else if (scale_fmt == CUTIE_SCALE_E8M0) {
       if (scale->element_size() != 1) bad("e8m0 scales must be 1-byte elements");
     } else if (scale->scalar_type() != at::kFloat) {
       bad("fp32 / pow2 scales must be float32");

@@ -16,7 +16,7 @@ from __future__ import annotations
 
 import torch
 
-from .layouts import SCALE_FORMATS, SCALE_LAYOUTS, mx_swizzled_size, n_groups
+from .layouts import SCALE_FORMATS, SCALE_LAYOUTS, mx_swizzled_size, n_groups, packed_ld
 from .ops import FP8_DTYPE, launch_rms_norm_fp8
 
 E8M0_DTYPE = getattr(torch, "float8_e8m0fnu", torch.uint8)
@@ -29,12 +29,21 @@ def empty_scale(M: int, H: int, group_size: int | None, scale_format: str = "fp3
     row: [M, G] row-major. col: a [M, G] view with strides (1, M) over a
     [G, M] buffer (``.t()`` gives the [G, M] tensor a blockwise FP8 GEMM
     reads). mx: flat e8m0 buffer of ceil(M/128)*128 * ceil(G/4)*4 bytes.
+    packed (e8m0 only): an int32 [M, ceil(G/4)] view with strides (1, ld),
+    ld = M rounded up to 4, four exponents a word (thingy_b200.layouts).
     """
     if scale_format not in SCALE_FORMATS:
         raise ValueError(f"scale_format must be one of {SCALE_FORMATS}")
     if scale_layout not in SCALE_LAYOUTS:
         raise ValueError(f"scale_layout must be one of {SCALE_LAYOUTS}")
     G = n_groups(H, group_size)
+    if scale_layout == "packed":
+        if scale_format != "e8m0":
+            raise ValueError("the packed scale layout needs scale_format='e8m0'")
+        W = (G + 3) // 4
+        # the unwritten pad bytes of the last word start at zero
+        alloc = torch.zeros if G % 4 else torch.empty
+        return alloc((W, packed_ld(M)), dtype=torch.int32, device=device).t()[:M]
     dtype = E8M0_DTYPE if scale_format == "e8m0" else torch.float32
     if scale_layout == "mx":
         return torch.empty(mx_swizzled_size(M, G), dtype=dtype, device=device)

@@ -24,7 +24,8 @@ except ImportError:  # the ctypes path below covers the same entry points
 from .layouts import SCALE_FORMATS, SCALE_LAYOUTS, mx_swizzled_size, n_groups
 
 _FMT_CODE = {"fp32": _lib.SCALE_FP32, "ue8m0": _lib.SCALE_FP32_POW2, "e8m0": _lib.SCALE_E8M0}
-_LAYOUT_CODE = {"row": _lib.LAYOUT_ROW_MAJOR, "col": _lib.LAYOUT_COL_MAJOR, "mx": _lib.LAYOUT_MX_SWIZZLED}
+_LAYOUT_CODE = {"row": _lib.LAYOUT_ROW_MAJOR, "col": _lib.LAYOUT_COL_MAJOR,
+                "mx": _lib.LAYOUT_MX_SWIZZLED, "packed": _lib.LAYOUT_COL_MAJOR_PACKED}
 
 E8M0_DTYPES = tuple(
     d for d in (getattr(torch, "float8_e8m0fnu", None), torch.uint8) if d is not None
@@ -71,10 +72,36 @@ def _check_x(x: torch.Tensor, dtype=torch.bfloat16) -> tuple[int, int]:
     return x.shape[0], x.shape[1]
 
 
+def _packed_scale_ld(scale: torch.Tensor, M: int, G: int, fmt: str, device) -> int:
+    """ld_scale (in int32 words) of a packed UE8M0 scale tensor."""
+    if fmt != "e8m0":
+        raise ValueError("the packed scale layout needs e8m0 scales")
+    if scale.dtype != torch.int32:
+        raise ValueError(f"packed e8m0 scales must be int32 words, got {scale.dtype}")
+    if scale.device != device:
+        raise ValueError(f"scale is on {scale.device}, expected {device}")
+    W = (G + 3) // 4
+    if scale.dim() == 1 and W == 1:
+        if scale.shape[0] != M or (M > 1 and scale.stride(0) != 1):
+            raise ValueError(f"packed per-row scales must be a contiguous [{M}] tensor")
+        return M
+    if scale.dim() == 2:
+        shape = tuple(scale.shape)
+        if shape == (M, W) and (M <= 1 or scale.stride(0) == 1):
+            return max(scale.stride(1), M) if W > 1 else M
+        if shape == (W, M) and (M <= 1 or scale.stride(1) == 1):
+            return max(scale.stride(0), M) if W > 1 else M
+    raise ValueError(
+        f"packed scales must be an int32 [{M}, {W}] tensor contiguous along M (or its transpose)"
+    )
+
+
 def _scale_args(scale: torch.Tensor, M: int, H: int, group_size: int | None, fmt: str,
                 layout: str, device) -> int:
     """Validate the scale tensor for (fmt, layout); return ld_scale."""
     G = n_groups(H, group_size)
+    if layout == "packed":
+        return _packed_scale_ld(scale, M, G, fmt, device)
     if fmt == "e8m0":
         if scale.dtype not in E8M0_DTYPES:
             raise ValueError(f"e8m0 scales must be uint8 or float8_e8m0fnu, got {scale.dtype}")
