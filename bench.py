@@ -49,8 +49,8 @@ def _kernel_name(w, threads_per_row) -> str:
     """The kernel that carries the timed step (the launch shape rules of csrc/capi.cu)."""
     if w.kind == "rms_f32":
         return "rmsnorm_f32_kernel"
-    if w.kind == "bwd":  # rows of up to 8192 take the bulk-copy ring variant
-        return "rmsnorm_backward_ring_kernel" if w.H <= 8192 else "rmsnorm_backward_kernel"
+    if w.kind == "bwd":  # rows of up to 16384 take the bulk-copy ring variant
+        return "rmsnorm_backward_ring_kernel" if w.H <= 16384 else "rmsnorm_backward_kernel"
     if threads_per_row == 32:
         return "rowwarp_rmsnorm_fp8_kernel"
     if w.group_size is None:  # per-token scaling: the single-pass kernel

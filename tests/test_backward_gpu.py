@@ -114,7 +114,10 @@ def _check_dw(dw_gpu, d):
     assert bool((err <= bound).all()), float((err - bound).max())
 
 
-SHAPES = [(64, 1024), (300, 7168), (129, 8192), (33, 200), (7, 4096), (1, 5120), (260, 3000)]
+# up to 8192: the ring kernel, two CTAs an SM; 12288 and 16384: the ring
+# kernel, one 384- / 512-thread CTA an SM; 20480 and 32768: the direct kernel
+SHAPES = [(64, 1024), (300, 7168), (129, 8192), (33, 200), (7, 4096), (1, 5120), (260, 3000),
+          (300, 12288), (150, 16384), (40, 20480), (17, 32768)]
 
 
 @pytest.mark.parametrize("M,H", SHAPES)
@@ -130,7 +133,8 @@ def test_backward_random(M, H, residual):
     _check_dw(dw, d)
 
 
-@pytest.mark.parametrize("M,H", [(64, 1024), (100, 7168), (9, 200), (40, 8192)])
+@pytest.mark.parametrize("M,H", [(64, 1024), (100, 7168), (9, 200), (40, 8192), (200, 16384),
+                                 (30, 32768)])
 @pytest.mark.parametrize("residual", [False, True])
 def test_backward_exact_sums_bitexact(M, H, residual):
     d = _inputs(M, H, residual, seed=M + H, exact=True)
@@ -142,7 +146,7 @@ def test_backward_exact_sums_bitexact(M, H, residual):
 
 @pytest.mark.parametrize("fmt,layout", [("fp32", "row"), ("fp32", "col"), ("ue8m0", "row"),
                                         ("e8m0", "row"), ("e8m0", "mx"), ("e8m0", "packed")])
-@pytest.mark.parametrize("M,H", [(256, 7168), (70, 1000)])
+@pytest.mark.parametrize("M,H", [(256, 7168), (70, 1000), (160, 16384), (20, 24576)])
 def test_backward_fp8_quant_of_dx(fmt, layout, M, H):
     d = _inputs(M, H, True, seed=7 * M + H)
     dx, _, q, s = _gpu_backward(d, quantize=True, scale_format=fmt, scale_layout=layout)

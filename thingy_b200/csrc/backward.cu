@@ -68,8 +68,8 @@ __device__ __forceinline__ void st_bf16x8(void* p, const uint32_t (&v)[4], bool 
   st_stream_if(ok, p, v);
 }
 
-// The direct kernel serves rows wider than 8192 (more than 256 threads; the
-// ring kernel below takes the rest). MAXT: the largest block of the
+// The direct kernel serves rows wider than 16384 (more than 512 threads;
+// the ring kernel below takes the rest). MAXT: the largest block of the
 // instantiation; 1024 caps the registers at 64 a thread.
 template <bool RES, bool QUANT, bool DW, bool FULL, int MAXT>
 __global__ void __launch_bounds__(MAXT, MAXT <= 256 ? 2 : 1)
@@ -253,7 +253,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 256 ? 2 : 1)
   }
 }
 
-// Bulk-copy ring variant of the kernel above (rows of up to 8192, 256
+// Bulk-copy ring variant of the kernel above (rows of up to 16384, 512
 // threads): the same arithmetic in the same order, with the loads moved off
 // the threads. Dynamic shared memory holds S stages of [r row | dn row |
 // dro row], each row buffer bwd_row_pad() bytes (the bytes past the copied
@@ -276,8 +276,10 @@ __host__ __device__ inline uint32_t bwd_row_pad(int V, int T) {
   return span > row_bytes ? span : row_bytes;
 }
 
-template <bool RES, bool QUANT, bool DW, bool FULL>
-__global__ void __launch_bounds__(256, 2)
+// MAXT: the largest block of the instantiation: 256 (two CTAs an SM) or 512
+// (one), up to 128 registers a thread either way.
+template <bool RES, bool QUANT, bool DW, bool FULL, int MAXT>
+__global__ void __launch_bounds__(MAXT, MAXT <= 256 ? 2 : 1)
     rmsnorm_backward_ring_kernel(const BwdArgs a, float eps, float rcp_H, int S) {
   constexpr int NV = 4;
   constexpr uint32_t NB = RES ? 3u : 2u;  // row buffers a stage
@@ -552,12 +554,12 @@ namespace {
 constexpr size_t kSmemPerSm = 228 * 1024;
 constexpr size_t kCtaSmemOverhead = 2048;
 
-// CTAs an SM runs at once: the ring kernel is compiled for two 256-thread
-// CTAs an SM (up to 128 registers a thread: 512 threads' worth of the 64K
-// registers), the direct kernel (MAXT = 1024) for 64 registers (1024
-// threads); at most 8 CTAs an SM either way.
+// CTAs an SM runs at once: the ring kernel is compiled for up to 128
+// registers a thread (512 threads' worth of the 64K registers: two CTAs of up
+// to 256 threads, or one of up to 512), the direct kernel (MAXT = 1024) for
+// 64 registers (1024 threads); at most 8 CTAs an SM either way.
 int backward_ctas_per_sm(int T) {
-  int per_sm = T <= 256 ? 512 / T : 1024 / T;
+  int per_sm = T <= 512 ? 512 / T : 1024 / T;
   if (per_sm < 1) per_sm = 1;
   if (per_sm > 8) per_sm = 8;
   return per_sm;
@@ -566,7 +568,7 @@ int backward_ctas_per_sm(int T) {
 // Stages of the ring kernel that fit next to per_sm - 1 other CTAs (0: the
 // ring does not fit).
 int backward_ring_stages(int V, int T, int per_sm, bool res) {
-  if (T > 256) return 0;
+  if (T > 512) return 0;
   const size_t stage = (res ? 3u : 2u) * (size_t)bwd_row_pad(V, T);
   size_t budget = kSmemPerSm / (size_t)per_sm;
   budget = budget > kCtaSmemOverhead ? budget - kCtaSmemOverhead : 0;
@@ -587,8 +589,8 @@ cudaError_t launch_with_smem(K k, int grid, int threads, size_t smem, cudaStream
   return launch_pdl(k, (unsigned)grid, (unsigned)threads, smem, st, args...);
 }
 
-// Rows of up to 8192 (T <= 256): the ring kernel; wider rows: the direct
-// kernel (MAXT = 1024).
+// Rows of up to 16384 (T <= 512): the ring kernel (MAXT 256 or 512); wider
+// rows: the direct kernel (MAXT = 1024).
 template <bool RES, bool QUANT, bool DW>
 cudaError_t launch_bwd3(const BwdArgs& a, float eps, int threads, int grid, int stages,
                         size_t direct_smem, cudaStream_t st) {
@@ -596,9 +598,14 @@ cudaError_t launch_bwd3(const BwdArgs& a, float eps, int threads, int grid, int 
   const float rcp_H = 1.0f / (float)a.qa.H;
   if (stages > 0) {
     const size_t smem = (size_t)stages * (RES ? 3u : 2u) * bwd_row_pad(a.qa.V, threads);
-    return full ? launch_with_smem(rmsnorm_backward_ring_kernel<RES, QUANT, DW, true>, grid,
+    if (threads <= 256)
+      return full ? launch_with_smem(rmsnorm_backward_ring_kernel<RES, QUANT, DW, true, 256>,
+                                     grid, threads, smem, st, a, eps, rcp_H, stages)
+                  : launch_with_smem(rmsnorm_backward_ring_kernel<RES, QUANT, DW, false, 256>,
+                                     grid, threads, smem, st, a, eps, rcp_H, stages);
+    return full ? launch_with_smem(rmsnorm_backward_ring_kernel<RES, QUANT, DW, true, 512>, grid,
                                    threads, smem, st, a, eps, rcp_H, stages)
-                : launch_with_smem(rmsnorm_backward_ring_kernel<RES, QUANT, DW, false>, grid,
+                : launch_with_smem(rmsnorm_backward_ring_kernel<RES, QUANT, DW, false, 512>, grid,
                                    threads, smem, st, a, eps, rcp_H, stages);
   }
   return full ? launch_with_smem(rmsnorm_backward_kernel<RES, QUANT, DW, true, 1024>, grid,
