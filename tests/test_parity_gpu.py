@@ -423,3 +423,28 @@ def test_back_to_back_launches_see_previous_outputs(M, H):
         for (q0, s0), (q1, s1) in zip(ref, got):
             assert torch.equal(q0.view(torch.uint8), q1.view(torch.uint8))
             assert torch.equal(s0, s1)
+
+
+@pytest.mark.parametrize("raw_stream", [False, True])
+def test_packed_scales_leading_dimension(raw_stream):
+    """Packed UE8M0 scales with a padded word stride (ld = 80 > M = 70), through
+    the torch binding and through the ctypes path (a raw stream handle): the
+    words of the M rows match the oracle's packing, the pad words are untouched."""
+    from thingy_b200.ops import launch_rms_norm_fp8
+
+    M, H, ld = 70, 7168, 80
+    W = 56 // 4
+    inp = exact_sum_inputs(M, H, residual=True, seed=21)
+    x, res, w = inp["x"].cuda(), inp["residual"].cuda(), inp["weight"].cuda()
+    buf = torch.full((W, ld), -1, dtype=torch.int32, device="cuda")
+    q = torch.empty(M, H, dtype=torch.float8_e4m3fn, device="cuda")
+    stream = torch.cuda.current_stream().cuda_stream if raw_stream else None
+    launch_rms_norm_fp8(x, w, 1e-6, residual=res, q=q, scale=buf.t()[:M], group_size=128,
+                        scale_format="e8m0", scale_layout="packed", stream=stream)
+    torch.cuda.synchronize()
+    q_ref, s_ref, _, _ = ora.rms_norm_fp8(inp["x"], inp["weight"], 1e-6,
+                                          residual=inp["residual"], scale_format="e8m0")
+    got = buf.cpu().numpy()
+    np.testing.assert_array_equal(got[:, :M], ora.layout_scales(s_ref, "packed")[:, :M])
+    assert (got[:, M:] == -1).all()
+    np.testing.assert_array_equal(q_codes(q), q_ref.numpy())
