@@ -133,7 +133,7 @@ def rms_norm_fp8_host(
             ev_drained[k].record(p.s_out)
     with torch.cuda.stream(p.s_out):
         p.s_out.wait_stream(p.s_run)
-        if scale_layout == "col":
+        if scale_layout in ("col", "packed"):  # strided [M, G] / [M, W] views
             scale.copy_(s_dev, non_blocking=True)
         else:
             scale.view(-1).copy_(s_dev.reshape(-1), non_blocking=True)
