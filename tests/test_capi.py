@@ -30,6 +30,20 @@ def test_header_declares_the_binding_table():
     assert sorted(declared_symbols()) == sorted(_lib.EXPORTED_SYMBOLS)
 
 
+def test_header_enums_match_the_python_constants():
+    """Every CUTIE_* enum value in the header equals the _lib constant of the
+    same name (CUTIE_ prefix dropped), and every such constant is in the header."""
+    text = HEADER.read_text()
+    enums = {m[0]: int(m[1]) for m in re.findall(r"\b(CUTIE_[A-Z0-9_]+)\s*=\s*(-?\d+)\s*,", text)}
+    assert len(enums) >= 17
+    for name, value in enums.items():
+        assert getattr(_lib, name[len("CUTIE_"):]) == value, name
+    prefixes = ("OK", "ERR_", "QUANT_", "SCALE_", "LAYOUT_", "DTYPE_")
+    for name in dir(_lib):
+        if name.startswith(prefixes) and isinstance(getattr(_lib, name), int):
+            assert "CUTIE_" + name in enums, name
+
+
 def test_exports_every_declared_symbol(lib):
     for name in declared_symbols():
         assert hasattr(lib, name), name
