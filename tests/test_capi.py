@@ -85,10 +85,43 @@ def fused(lib, **kw):
         ({"quant_mode": 0}, _lib.ERR_INVALID_ARGUMENT, "no output"),
         ({"scale_layout": 2}, _lib.ERR_INVALID_ARGUMENT, "E8M0"),
         ({"eps": float("nan")}, _lib.ERR_INVALID_ARGUMENT, "eps"),
+        ({"scale_layout": _lib.LAYOUT_COL_MAJOR_PACKED}, _lib.ERR_INVALID_ARGUMENT,
+         "packed scale layout needs E8M0"),
+        ({"scale_layout": _lib.LAYOUT_COL_MAJOR_PACKED, "scale_fmt": _lib.SCALE_E8M0,
+          "ld_scale": 3}, _lib.ERR_INVALID_ARGUMENT, "words < M"),
+        ({"scale_layout": 4}, _lib.ERR_INVALID_ARGUMENT, "scale_layout"),
     ],
 )
 def test_argument_errors(lib, kw, code, needle):
     assert fused(lib, **kw) == code
+    assert needle in lib.cutie_last_error().decode()
+
+
+def backward(lib, **kw):
+    args = dict(dn=FAKE, ldd=1024, r=FAKE, ldr=1024, weight=FAKE, dro=None, lddr=0, eps=1e-6,
+                M=4, H=1024, dx=FAKE, lddx=1024, d_weight=None, workspace=None,
+                workspace_bytes=ctypes.c_size_t(0), quant_mode=_lib.QUANT_GROUP, group_size=128,
+                scale_fmt=0, scale_layout=0, ld_scale=0, q=FAKE, ldq=1024, scale=FAKE,
+                stream=None)
+    args.update(kw)
+    return lib.cutie_rms_norm_backward(*args.values())
+
+
+@pytest.mark.parametrize(
+    "kw,code,needle",
+    [
+        ({"H": 40000, "ldd": 40000, "ldr": 40000, "lddx": 40000, "ldq": 40000},
+         _lib.ERR_UNSUPPORTED, "32768"),
+        ({"group_size": 32}, _lib.ERR_UNSUPPORTED, "1x128 groups only"),
+        ({"scale_layout": _lib.LAYOUT_COL_MAJOR_PACKED}, _lib.ERR_INVALID_ARGUMENT,
+         "packed scale layout needs E8M0"),
+        ({"scale_layout": _lib.LAYOUT_COL_MAJOR_PACKED, "scale_fmt": _lib.SCALE_E8M0,
+          "ld_scale": 3}, _lib.ERR_INVALID_ARGUMENT, "words < M"),
+        ({"scale_layout": 4}, _lib.ERR_INVALID_ARGUMENT, "scale_layout"),
+    ],
+)
+def test_backward_argument_errors(lib, kw, code, needle):
+    assert backward(lib, **kw) == code
     assert needle in lib.cutie_last_error().decode()
 
 
