@@ -39,6 +39,11 @@ def test_workload_bytes_match_the_traffic_model():
     assert [WORKLOADS["mx32_decode_5120"].bytes_moved(m) for m in (1, 8, 32, 128)] == [
         25_760, 134_400, 506_880, 1_996_800]
     assert WORKLOADS["g128_sharded_262144x8192"].bytes_moved() == 6_509_576_192
+    # backward: d_normalized, r, d_residual_out read, dx written (4 x 2MH), weight read
+    # and d_weight written (2 x 2H), FP8 codes of dx (MH) and fp32 scales (4 M H/128)
+    M, H = 16384, 7168
+    assert WORKLOADS["bwd_residual_g128_16384x7168"].bytes_moved() == (
+        8 * M * H + 4 * H + M * H + 4 * M * (H // 128)) == 1_060_663_296
 
 
 def test_inputs_are_seeded_and_shaped():
