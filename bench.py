@@ -3,13 +3,16 @@
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
                   [--workload NAME] [--threads-per-row T]
 
-A step is one pass of the path over one batch of the workload (default
-g128_16384x7168: x bf16 [16384, 7168] with outlier channels, 1x128 groups,
-fp32 column-major scales, no residual). Under torchrun (N > 1) every rank
-processes its own batch on its own GPU (weak scaling, no data-path
-collective; NCCL carries only the barrier and the max-over-ranks time).
-The sharded workload g128_sharded_262144x8192 instead splits one fixed
-262144-row batch over the ranks (strong scaling).
+A step is one pass of the path over one batch of the workload. The default
+workload is g128_sharded_262144x8192 (x bf16 [262144, 8192] with outlier
+channels, 1x128 groups, fp32 column-major scales, no residual), the one
+configuration defined at 1, 2, 4 and 8 GPUs: under torchrun (N > 1) the
+262144 rows are split evenly by rows over the ranks (strong scaling), every
+rank processing its own contiguous shard on its own GPU with no data-path
+collective (NCCL carries only the barrier and the max-over-ranks time). At
+N = 1 the same line also carries, under "secondary", the device-timed
+measurement of g128_16384x7168 (the DeepSeek-V3 shape, 16384 rows). Other
+workloads (--workload) run as weak scaling: every rank its own full batch.
 
 value: algorithmic HBM bytes of all ranks / max-over-ranks device time of K
 steps with inputs resident in HBM; consecutive steps rotate through enough
@@ -19,7 +22,8 @@ the H2D copy of x and the D2H copy of q and scales inside the timed region.
 roofline: bytes per launch / mean per-launch device time (CUDA events on the
 launch stream) against MEASURED_PEAKS.json's HBM copy bandwidth.
 cpu_baseline / --impl reference: the reference's PyTorch path (restated in
-oracle/reference.py) on the host cores, on a bounded row sample.
+oracle/reference.py) on the host cores, on a bounded row sample; this arm
+imports no module that loads the CUDA library.
 """
 
 from __future__ import annotations
@@ -42,6 +46,8 @@ sys.path.insert(0, str(REPO))
 METRIC = "fused RMSNorm+FP8 quant HBM GB/s & % of B200 peak; tokens/s at 1/2/4/8 GPU"
 L2_BYTES = 126 * 1024 * 1024
 FALLBACK_HBM_GBS = 6650.0
+DEFAULT_WORKLOAD = "g128_sharded_262144x8192"  # BASELINE config 5, defined at 1/2/4/8 GPUs
+SECONDARY_WORKLOAD = "g128_16384x7168"         # BASELINE config 2, device-timed at N = 1
 
 
 
@@ -63,7 +69,8 @@ def parse_args():
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
-    ap.add_argument("--workload", default="g128_16384x7168")
+    ap.add_argument("--workload", default=None,
+                    help=f"default {DEFAULT_WORKLOAD} (strong scaling over the ranks)")
     ap.add_argument("--threads-per-row", type=int, default=0)
     ap.add_argument("--e2e-steps", type=int, default=0, help="0: min(steps, 20)")
     ap.add_argument("--no-e2e", action="store_true")
@@ -79,6 +86,8 @@ def parse_args():
         ap.error("--warmup must be >= 3")
     if args.steps < 1:
         ap.error("--steps must be >= 1")
+    args.secondary = args.workload is None
+    args.workload = args.workload or DEFAULT_WORKLOAD
     return args
 
 
@@ -199,6 +208,39 @@ def workload_rows(w, world: int, rank: int):
     return w.M, "weak"
 
 
+def n_workspaces(w, M) -> int:
+    """Workspaces rotated between steps so a step never finds its data in L2."""
+    return max(2, math.ceil(3 * L2_BYTES / w.bytes_moved(M)))
+
+
+def bench_config(args, w, M: int, world: int, scaling: str) -> dict:
+    """The `config` object of the JSON line; both arms emit exactly this."""
+    bytes_step = w.bytes_moved(M)
+    n_ws = n_workspaces(w, M)
+    return {
+        "workload": w.name,
+        "rows_per_gpu": M,
+        "rows_total": w.M if scaling == "strong" else world * M,
+        "H": w.H,
+        "group_size": w.group_size or "per-token",
+        "scale_format": w.scale_format,
+        "scale_layout": w.scale_layout,
+        "residual": w.residual,
+        "parallelism": (f"row shards, dp{world}, "
+                        + ("one batch split by rows" if scaling == "strong"
+                           else "a full batch per rank") + ", no data-path collective"),
+        "l2": f"rotating {n_ws} workspaces of {bytes_step / 1e6:.1f} MB "
+              f"({n_ws * bytes_step / 1e6:.0f} MB > L2 {L2_BYTES / 1e6:.0f} MB)",
+        "threads_per_row": args.threads_per_row or "auto",
+        "launch": "one CUDA graph of the K launches" if args.graph else "eager launches",
+    }
+
+
+def dtype_of(w) -> str:
+    return ("bf16 gradients, fp32 sums, e4m3 dx" if w.kind == "bwd"
+            else "bf16 in, fp32 statistics, e4m3 out")
+
+
 class Workspace:
     """One set of device inputs and outputs for a step."""
 
@@ -232,31 +274,18 @@ class Workspace:
         self.res_out = torch.empty_like(self.x) if self.res is not None else None
 
 
-def run_ours(args, rank, world, local_rank):
-    import thingy_b200 as tb
-    from thingy_b200 import _lib
-    from thingy_b200.host import rms_norm_fp8_host
-    from thingy_b200.ops import launch_rms_norm_fp8
-    from thingy_b200.shard import max_over_ranks
-    from thingy_b200.workloads import WORKLOADS, make_inputs
+def device_run(args, w, M, src, device, local_rank, world, K):
+    """W warm-up steps, then K timed steps (CUDA events on the launch stream).
+
+    Returns (per-step ms of this rank, clock summary or None)."""
+    from thingy_b200.ops import launch_rms_norm, launch_rms_norm_backward, launch_rms_norm_fp8
 
     import torch.distributed as dist
 
-    device = torch.device("cuda", local_rank)
-    torch.cuda.set_device(device)
-    _lib.load()
-    w = WORKLOADS[args.workload]
-    M, scaling = workload_rows(w, world, rank)
-    src = make_inputs(w, M, device=device, seed=0, row_offset=rank)
     weight = src["weight"]
-    bytes_step = w.bytes_moved(M)
-    n_ws = max(2, math.ceil(3 * L2_BYTES / bytes_step))
+    n_ws = n_workspaces(w, M)
     ws = [Workspace(w, M, src, device) for _ in range(n_ws)]
     stream = torch.cuda.current_stream(device)
-
-    from thingy_b200.ops import launch_rms_norm
-
-    from thingy_b200.ops import launch_rms_norm_backward
 
     def step(i):  # one launch on the current stream
         s = ws[i % n_ws]
@@ -283,9 +312,8 @@ def run_ours(args, rank, world, local_rank):
         step(i)
     torch.cuda.synchronize(device)
 
-    K = args.steps
-    starts = [torch.cuda.Event(enable_timing=True)]
-    ends = [torch.cuda.Event(enable_timing=True)]
+    start = torch.cuda.Event(enable_timing=True)
+    end = torch.cuda.Event(enable_timing=True)
     graph = None
     if args.graph:
         # the same K launches recorded once; timed by events around the replay
@@ -302,23 +330,23 @@ def run_ours(args, rank, world, local_rank):
     # K launches back to back (no event between them, so a launch's prologue
     # may overlap the previous one's tail through programmatic dependent
     # launch); the mean launch is the timed region over K.
-    starts[0].record(stream)
+    start.record(stream)
     if graph is not None:
         graph.replay()
     else:
         for i in range(K):
             step(i)
-    ends[-1].record(stream)
+    end.record(stream)
     torch.cuda.synchronize(device)
     if clocks:
         clocks.stop()
     barrier()
-    total_ms = starts[0].elapsed_time(ends[-1])
-    launch_ms = total_ms / K
+    total_ms = start.elapsed_time(end)
     window = "timed"
     if clocks and len(clocks.samples) < 5:
         # The timed region was too short for the sampler: keep the same launches
         # running for ~1 s more (untimed) so the clock record covers the load.
+        # Every rank soaks for the same wall time and meets at the barrier.
         t_end = time.monotonic() + 1.0
         clocks.start()
         i = 0
@@ -329,15 +357,62 @@ def run_ours(args, rank, world, local_rank):
             torch.cuda.synchronize(device)
         clocks.stop()
         window = "timed+1s untimed soak (timed region shorter than the sampler period)"
-    t_step_ms = max_over_ranks(total_ms / K, device) if world > 1 else total_ms / K
-    launch_ms_max = max_over_ranks(launch_ms, device) if world > 1 else launch_ms
+    barrier()
+    del graph, ws
+    return total_ms / K, (clocks.summary(window) if clocks else None)
 
-    value = world * bytes_step / (t_step_ms * 1e-3) / 1e9 if scaling == "weak" else (
-        w.bytes_moved() + 2 * w.H * (world - 1)) / (t_step_ms * 1e-3) / 1e9
-    rows_total = world * M if scaling == "weak" else w.M
+
+def roofline(w, bytes_step, launch_ms, threads_per_row) -> dict:
     peak, peak_src = measured_peak()
-    achieved = bytes_step / (launch_ms_max * 1e-3) / 1e9
+    achieved = bytes_step / (launch_ms * 1e-3) / 1e9
     traffic, traffic_src = ncu_traffic(w.name)
+    return {
+        "bound": "hbm",
+        "achieved": round(achieved, 2),
+        "peak": peak,
+        "unit": "GB/s",
+        "frac": round(achieved / peak, 4),
+        "traffic": traffic,
+        "traffic_source": traffic_src,
+        "peak_source": peak_src,
+        "kernel": _kernel_name(w, threads_per_row),
+        "bytes_per_launch": bytes_step,
+        "mean_launch_ms": round(launch_ms, 5),
+    }
+
+
+def run_ours(args, rank, world, local_rank):
+    import thingy_b200 as tb
+    from thingy_b200 import _lib
+    from thingy_b200.host import rms_norm_fp8_host
+    from thingy_b200.shard import max_over_ranks
+    from thingy_b200.workloads import WORKLOADS, make_inputs
+
+    import torch.distributed as dist
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    _lib.load()
+    w = WORKLOADS[args.workload]
+    M, scaling = workload_rows(w, world, rank)
+    src = make_inputs(w, M, device=device, seed=0, row_offset=rank)
+    weight = src["weight"]
+    bytes_step = w.bytes_moved(M)
+    K = args.steps
+    step_ms, clocks = device_run(args, w, M, src, device, local_rank, world, K)
+    t_step_ms = max_over_ranks(step_ms, device) if world > 1 else step_ms
+
+    # all ranks' algorithmic bytes (strong scaling: the whole batch, plus one
+    # weight read per extra rank) over the slowest rank's step time
+    total_bytes = world * bytes_step if scaling == "weak" else (
+        w.bytes_moved() + 2 * w.H * (world - 1))
+    value = total_bytes / (t_step_ms * 1e-3) / 1e9
+    rows_total = world * M if scaling == "weak" else w.M
+    peak, _ = measured_peak()
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
 
     # e2e through the host-buffer API: pinned host x in, q + scales out
     e2e = None
@@ -351,6 +426,7 @@ def run_ours(args, rank, world, local_rank):
         roh = torch.empty_like(xh).pin_memory() if rh is not None else None
         pipe = None
         chunk = 2048
+        stream = torch.cuda.current_stream(device)
 
         def e2e_step():
             nonlocal pipe
@@ -377,8 +453,7 @@ def run_ours(args, rank, world, local_rank):
         d2h = qh.numel() + sh.numel() * sh.element_size() + (
             roh.numel() * 2 if roh is not None else 0)
         e2e = {
-            "value": round(world * bytes_step / (e2e_ms * 1e-3) / 1e9, 3)
-            if scaling == "weak" else round(w.bytes_moved() / (e2e_ms * 1e-3) / 1e9, 3),
+            "value": round(total_bytes / (e2e_ms * 1e-3) / 1e9, 3),
             "unit": "GB/s",
             "ms_per_step": round(e2e_ms, 4),
             "steps": K2,
@@ -387,10 +462,34 @@ def run_ours(args, rank, world, local_rank):
             "api": "thingy_b200.host.rms_norm_fp8_host (pinned host buffers, "
                    f"{chunk}-row chunks over 3 streams)",
         }
+        del xh, rh, qh, sh, roh, pipe
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and w.kind == "fused":
         cpu = cpu_baseline(w, args.cpu_seconds)
+
+    # N = 1 with the default workload: also time BASELINE config 2 (the
+    # DeepSeek-V3 shape) on the device, same rules, so its roofline is on record
+    secondary = None
+    if args.secondary and world == 1:
+        del src
+        torch.cuda.empty_cache()
+        w2 = WORKLOADS[SECONDARY_WORKLOAD]
+        src2 = make_inputs(w2, device=device, seed=0)
+        ms2, clocks2 = device_run(args, w2, w2.M, src2, device, local_rank, 1, K)
+        del src2
+        b2 = w2.bytes_moved()
+        secondary = {
+            "workload": w2.name,
+            "value": round(b2 / (ms2 * 1e-3) / 1e9, 2),
+            "unit": "GB/s",
+            "ms_per_step": round(ms2, 5),
+            "steps": K,
+            "tokens_per_s": round(w2.M / (ms2 * 1e-3), 1),
+            "config": bench_config(args, w2, w2.M, 1, "weak"),
+            "roofline": roofline(w2, b2, ms2, args.threads_per_row),
+            "clocks": clocks2,
+        }
 
     result = {
         "metric": METRIC,
@@ -403,44 +502,20 @@ def run_ours(args, rank, world, local_rank):
         "higher_is_better": True,
         "scaling": scaling,
         "vs_baseline": None,
-        "dtype": ("bf16 gradients, fp32 sums, e4m3 dx" if w.kind == "bwd"
-                  else "bf16 in, fp32 statistics, e4m3 out"),
+        "dtype": dtype_of(w),
         "data": "synthetic (seeded; shapes and distributions of the workload)",
-        "config": {
-            "workload": w.name,
-            "rows_per_gpu": M,
-            "H": w.H,
-            "group_size": w.group_size or "per-token",
-            "scale_format": w.scale_format,
-            "scale_layout": w.scale_layout,
-            "residual": w.residual,
-            "parallelism": f"row shards, dp{world}, no data-path collective",
-            "l2": f"rotating {n_ws} workspaces of {bytes_step / 1e6:.1f} MB "
-                  f"({n_ws * bytes_step / 1e6:.0f} MB > L2 {L2_BYTES / 1e6:.0f} MB)",
-            "threads_per_row": args.threads_per_row or "auto",
-            "launch": "one CUDA graph of the K launches" if args.graph else "eager launches",
-        },
+        "config": bench_config(args, w, M, world, scaling),
         "tokens_per_s": round(rows_total / (t_step_ms * 1e-3), 1),
         "pct_of_hbm_peak": round(100 * value / (peak * world), 2),
         "pct_of_8tbs": round(100 * value / (8000.0 * world), 2),
-        "roofline": {
-            "bound": "hbm",
-            "achieved": round(achieved, 2),
-            "peak": peak,
-            "unit": "GB/s",
-            "frac": round(achieved / peak, 4),
-            "traffic": traffic,
-            "traffic_source": traffic_src,
-            "peak_source": peak_src,
-            "kernel": _kernel_name(w, args.threads_per_row),
-            "bytes_per_launch": bytes_step,
-            "mean_launch_ms": round(launch_ms_max, 5),
-        },
+        "roofline": roofline(w, bytes_step, t_step_ms, args.threads_per_row),
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": K * (2 if w.kind == "bwd" else 1),
-        "clocks": clocks.summary(window) if clocks else None,
+        "clocks": clocks,
     }
+    if secondary is not None:
+        result["secondary"] = secondary
     if rank == 0:
         print(json.dumps(result), flush=True)
 
@@ -508,23 +583,27 @@ def cpu_model() -> str:
 
 
 def run_reference(args, rank, world):
-    """The reference's PyTorch path on the host cores (oracle/reference.py restates it)."""
+    """The reference's PyTorch path on the host cores (oracle/reference.py restates it).
+
+    Imports only pure-Python modules of the package (workloads, shard): the
+    CUDA library and the torch binding are never loaded by this arm."""
     if rank != 0:
         return
     from thingy_b200.workloads import WORKLOADS
 
     w = WORKLOADS[args.workload]
+    M, scaling = workload_rows(w, world, rank)
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     # bounded sample per step so W + K steps finish in a few minutes
     per_step_s = min(2.0, 150.0 / max(1, args.steps + args.warmup))
-    rows = cpu_sample_rows(w, 4 * per_step_s, threads)
+    rows = min(M, cpu_sample_rows(w, 4 * per_step_s, threads))
     time_oracle(w, rows, args.warmup)
     times = time_oracle(w, rows, args.steps)
     t = sum(times) / len(times)
     value = w.bytes_moved(rows) / t / 1e9
-    sample = (f"{rows} of {w.M} rows of {w.name} per step, torch CPU ops as in the "
-              "reference's PyTorch path (oracle/reference.py)")
+    sample = (f"{rows} of the {M} rows of one rank of {w.name} per step, torch CPU ops "
+              "as in the reference's PyTorch path (oracle/reference.py), rank 0 only")
     print(json.dumps({
         "impl": "reference",
         "metric": METRIC,
@@ -535,15 +614,11 @@ def run_reference(args, rank, world):
         "warmup": args.warmup,
         "ms_per_step": round(t * 1e3, 3),
         "higher_is_better": True,
-        "scaling": "weak",
+        "scaling": scaling,
         "vs_baseline": None,
-        "dtype": ("bf16 gradients, fp32 sums, e4m3 dx" if w.kind == "bwd"
-                  else "bf16 in, fp32 statistics, e4m3 out"),
+        "dtype": dtype_of(w),
         "data": "synthetic (seeded; shapes and distributions of the workload)",
-        "config": {"workload": w.name, "rows_per_step": rows, "H": w.H,
-                   "group_size": w.group_size or "per-token", "scale_format": w.scale_format,
-                   "scale_layout": w.scale_layout, "residual": w.residual,
-                   "parallelism": "host CPU, rank 0 only"},
+        "config": bench_config(args, w, M, world, scaling),
         "tokens_per_s": round(rows / t, 1),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": torch.get_num_threads(),
                          "kind": "port", "sample": sample, "cpu": cpu_model()},

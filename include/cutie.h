@@ -208,11 +208,14 @@ CUTIE_API size_t cutie_rms_norm_backward_workspace(int64_t M, int64_t H);
  * CUTIE_ERR_UNSUPPORTED. Every row of the array that a call reads was
  * written by that call, so nothing needs clearing between calls.
  *
- * The first call on a device looks up the array's device address there
- * (once per device, with that device current); make that first call before
- * any stream capture. All calls on a device share the one array, so calls
- * that may run at the same time on the GPU (other streams, other host
- * threads) race on it and give wrong d_weight: order them on one stream.
+ * Every call resolves the array's device address in the calling thread's
+ * current context (cudaGetSymbolAddress; nothing is cached, so the address
+ * stays right after cudaDeviceReset or under another driver context). The
+ * first call in a context also loads the library's device code there: make
+ * that first call before any stream capture. All calls on a device share the
+ * one array, so calls that may run at the same time on the GPU (other
+ * streams, other host threads) race on it and give wrong d_weight: order
+ * them on one stream.
  */
 CUTIE_API int cutie_rms_norm_backward_noalloc(const void* d_normalized, int64_t ldd,
                                               const void* r, int64_t ldr, const void* weight,
@@ -228,12 +231,26 @@ CUTIE_API int cutie_rms_norm_backward_noalloc(const void* d_normalized, int64_t 
  * no kernel has hit a failure since the last clear; otherwise the first error
  * code recorded (1 = a bulk-copy wait ran out: a row never arrived in shared
  * memory within ~2 s and the kernel stopped early, leaving outputs
- * incomplete; 2 = a kernel was launched with a shared-memory ring depth it
- * does not hold and wrote nothing). Synchronises with the device; `clear` != 0
+ * incomplete, see cutie_set_wait_limit; 2 = a kernel was launched with a
+ * shared-memory ring depth it does not hold and wrote nothing). Synchronises with the device; `clear` != 0
  * resets the word.
  * A negative return is a CUDA failure (see cutie_last_error()).
  */
 CUTIE_API int cutie_device_error(int clear);
+
+/*
+ * Limit, in SM clock cycles, on every wait that the kernels launched later
+ * by the calling thread make for their own bulk copies and row exchanges
+ * (the default, about 2 s, bounds a copy that never lands). A wait that runs
+ * out stops the kernel early with device error 1 (cutie_device_error); the
+ * kernel first lets the copies it issued land, so the GPU stays usable.
+ * cycles == 0 restores the default; cycles < 0 makes every wait that would
+ * have to block give up at once, which exercises that failure path with
+ * valid inputs (the outputs of such a launch are incomplete). Affects this
+ * thread only; returns the previous limit. No counterpart in the reference,
+ * whose kernels have no waits that can run out.
+ */
+CUTIE_API int64_t cutie_set_wait_limit(int64_t cycles);
 
 /* Message of the last failing call on this thread ("" if none). */
 CUTIE_API const char* cutie_last_error(void);

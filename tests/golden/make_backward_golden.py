@@ -2,13 +2,13 @@
 
 The reference has no backward pass; the gradients of its PyTorch forward are
 what torch autograd computes for it. This script imports the reference's
-unmodified bench.py (as make_golden.py does: same stub, same checkout, default
-/root/reference or REFERENCE_ROOT), differentiates its rms_norm_reference
+unmodified bench.py (as make_golden.py does: same stub, and the checkout named
+by the first argument or REFERENCE_ROOT), differentiates its rms_norm_reference
 (src/cutie/rms_norm/bench.py:58-65) and its residual add (x + residual, as in
 residual_rms_norm_fp8_reference, bench.py:97) with torch.autograd on the CPU,
 and stores inputs and gradients. Nothing at test time reads the reference.
 
-  python tests/golden/make_backward_golden.py
+  python tests/golden/make_backward_golden.py <reference-root>
 """
 
 from __future__ import annotations

@@ -1,10 +1,12 @@
 """Regenerate tests/golden/reference_vectors.npz from the reference's own code.
 
-Run in a container that has the reference checkout (default
-/root/reference, or REFERENCE_ROOT); the GPU box does not, and nothing at
-test time reads the reference — only the committed .npz.
+Run where a checkout of the reference exists, naming its root by argument
+or by the REFERENCE_ROOT environment variable (there is no default); the GPU
+box has no checkout, and nothing at test time reads the reference — only
+the committed .npz.
 
-  python tests/golden/make_golden.py
+  python tests/golden/make_golden.py <reference-root>
+  REFERENCE_ROOT=<reference-root> python tests/golden/make_golden.py
 
 What runs is the reference's own Python, unmodified:
   * src/cutie/rms_norm/bench.py: rms_norm_reference, residual_rms_norm_fp8_reference
@@ -32,11 +34,25 @@ os.environ["TRITON_INTERPRET"] = "1"
 import numpy as np  # noqa: E402
 import torch  # noqa: E402
 
-REF = Path(os.environ.get("REFERENCE_ROOT", "/root/reference"))
 OUT = Path(__file__).resolve().parent / "reference_vectors.npz"
 
 
+def reference_root() -> Path:
+    """The reference checkout: the first command-line argument, else REFERENCE_ROOT."""
+    args = [a for a in sys.argv[1:] if not a.startswith("-")]
+    root = args[0] if args else os.environ.get("REFERENCE_ROOT")
+    if not root:
+        raise SystemExit("name the reference checkout: make_golden.py <reference-root> "
+                         "(or set REFERENCE_ROOT)")
+    root = Path(root)
+    if not (root / "src" / "cutie" / "rms_norm" / "bench.py").exists():
+        raise SystemExit(f"{root} does not look like the reference checkout "
+                         "(src/cutie/rms_norm/bench.py is missing)")
+    return root
+
+
 def _import_reference():
+    REF = reference_root()
     stub = types.ModuleType("cutlass.testing")
     stub.JitArguments = object
     stub.benchmark = None

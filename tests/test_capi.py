@@ -125,6 +125,47 @@ def test_backward_argument_errors(lib, kw, code, needle):
     assert needle in lib.cutie_last_error().decode()
 
 
+def backward_noalloc(lib, **kw):
+    args = dict(dn=FAKE, ldd=1024, r=FAKE, ldr=1024, weight=FAKE, dro=None, lddr=0, eps=1e-6,
+                M=4, H=1024, dx=FAKE, lddx=1024, d_weight=None, quant_mode=_lib.QUANT_GROUP,
+                group_size=128, scale_fmt=0, scale_layout=0, ld_scale=0, q=FAKE, ldq=1024,
+                scale=FAKE, stream=None)
+    args.update(kw)
+    return lib.cutie_rms_norm_backward_noalloc(*args.values())
+
+
+MISALIGNED = ctypes.c_void_p(0x10008)  # 8-byte aligned only
+
+
+@pytest.mark.parametrize(
+    "kw,code,needle",
+    [
+        ({"H": 40000, "ldd": 40000, "ldr": 40000, "lddx": 40000, "ldq": 40000},
+         _lib.ERR_UNSUPPORTED, "32768"),
+        ({"H": 1020, "ldd": 1020, "ldr": 1020, "lddx": 1020, "ldq": 1020},
+         _lib.ERR_UNSUPPORTED, "multiple of 8"),
+        ({"r": MISALIGNED}, _lib.ERR_ALIGNMENT, "16-byte aligned"),
+        ({"dn": MISALIGNED}, _lib.ERR_ALIGNMENT, "16-byte aligned"),
+        ({"weight": MISALIGNED}, _lib.ERR_ALIGNMENT, "weight"),
+        ({"weight": None}, _lib.ERR_INVALID_ARGUMENT, "weight is NULL"),
+        ({"M": -1}, _lib.ERR_INVALID_ARGUMENT, "M >= 0"),
+        ({"group_size": 32}, _lib.ERR_UNSUPPORTED, "1x128 groups only"),
+        ({"scale_layout": 4}, _lib.ERR_INVALID_ARGUMENT, "scale_layout"),
+        ({"eps": float("inf")}, _lib.ERR_INVALID_ARGUMENT, "eps"),
+    ],
+)
+def test_backward_noalloc_argument_errors(lib, kw, code, needle):
+    """The allocation-free backward validates like the workspace one, before any CUDA call."""
+    assert backward_noalloc(lib, **kw) == code
+    assert needle in lib.cutie_last_error().decode()
+
+
+def test_backward_noalloc_nothing_to_do_is_a_no_op(lib):
+    """M = 0 with no d_weight requested returns at once, touching no device state."""
+    assert backward_noalloc(lib, M=0, dn=None, r=None, dx=None, q=None, scale=None) == _lib.OK
+    assert lib.cutie_last_error() == b""
+
+
 def test_empty_batch_is_a_no_op(lib):
     assert fused(lib, M=0, x=None, q=None, scale=None, weight=None) == _lib.OK
     assert lib.cutie_last_error() == b""
@@ -142,3 +183,21 @@ def test_quantizer_and_rms_norm_errors(lib):
 def test_python_maps_status_to_exceptions(lib):
     with pytest.raises(ValueError, match="multiple of 8"):
         _lib.check(fused(lib, H=1020, ldx=1020, ldq=1020))
+
+
+def test_wait_limit_is_per_thread_and_restorable(lib):
+    """cutie_set_wait_limit returns the previous limit, 0 restores the default
+    (~2 s of SM cycles), and the setting belongs to the calling thread."""
+    import threading
+
+    default = 4_000_000_000
+    assert lib.cutie_set_wait_limit(-1) == default
+    assert lib.cutie_set_wait_limit(0) == -1
+    assert lib.cutie_set_wait_limit(123) == default
+    seen = []
+    t = threading.Thread(target=lambda: seen.append(lib.cutie_set_wait_limit(0)))
+    t.start()
+    t.join()
+    assert seen == [default]  # the other thread never saw 123
+    assert lib.cutie_set_wait_limit(0) == 123
+    assert _lib.set_wait_limit(0) == default

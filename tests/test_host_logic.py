@@ -145,3 +145,29 @@ def test_packed_scale_allocation_and_validation():
     with pytest.raises(ValueError):  # row-contiguous is not the packed layout
         _scale_args(torch.zeros(10, 14, dtype=torch.int32), 10, 7168, 128, "e8m0", "packed",
                     torch.device("cpu"))
+
+
+def test_torch_library_ops_trace_with_fake_tensors():
+    """The ops a torch.compile region sees have fake implementations with the
+    real outputs' shapes and dtypes, including the reference's own op name
+    cutie::per_token_fp8_quant (registered when no module has claimed it)."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    import thingy_b200.custom_ops as co
+
+    assert co.REFERENCE_NAMESPACE_OP
+    with FakeTensorMode():
+        x = torch.empty(37, 7168, dtype=torch.bfloat16)
+        w = torch.empty(7168, dtype=torch.bfloat16)
+        y = torch.ops.thingy_b200.rms_norm(x, w, 1e-6)
+        assert (y.shape, y.dtype) == (x.shape, torch.bfloat16)
+        xf = torch.empty(5, 3072)
+        yf = torch.ops.thingy_b200.rms_norm(xf, torch.empty(3072), 1e-5)
+        assert (yf.shape, yf.dtype) == (xf.shape, torch.float32)
+        for op in (torch.ops.cutie.per_token_fp8_quant, torch.ops.thingy_b200.per_token_fp8_quant):
+            q, s = op(torch.empty(9, 200, dtype=torch.bfloat16))
+            assert (q.shape, q.dtype, s.shape, s.dtype) == (
+                (9, 200), torch.float8_e4m3fn, (9, 2), torch.float32)
+        q, s, r, n = torch.ops.thingy_b200.residual_rms_norm_fp8(x, x, w, 1e-6)
+        assert q.dtype == torch.float8_e4m3fn and s.shape == (37, 56)
+        assert r.shape == n.shape == x.shape

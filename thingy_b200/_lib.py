@@ -36,6 +36,7 @@ EXPORTED_SYMBOLS = (
     "cutie_rms_norm_backward_workspace",
     "cutie_rms_norm_backward_noalloc",
     "cutie_device_error",
+    "cutie_set_wait_limit",
     "cutie_last_error",
     "cutie_abi_version",
 )
@@ -71,6 +72,7 @@ _SIGNATURES = {
          _int, _int, _int, _int, _i64, _ptr, _i64, _ptr, _ptr],
     ),
     "cutie_device_error": (_int, [_int]),
+    "cutie_set_wait_limit": (_i64, [_i64]),
     "cutie_last_error": (ctypes.c_char_p, []),
     "cutie_abi_version": (_int, []),
 }
@@ -118,6 +120,15 @@ def device_error(clear: bool = True) -> int:
     if status < 0:
         check(status)
     return status
+
+
+def set_wait_limit(cycles: int) -> int:
+    """Bound every wait of this thread's later launches by ``cycles`` SM cycles.
+
+    0 restores the default (about 2 s); a negative value makes a wait that
+    would block give up at once (failure-path testing). Returns the previous
+    limit."""
+    return int(load().cutie_set_wait_limit(int(cycles)))
 
 
 def check(status: int) -> None:

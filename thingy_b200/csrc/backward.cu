@@ -29,7 +29,6 @@
 // the forward's two-groups-an-octet scheme.
 #include "launch.cuh"
 
-#include <mutex>
 
 namespace cutie {
 
@@ -38,26 +37,23 @@ namespace cutie {
 // per-CTA partial sums of d_weight go to this file-scope array instead of a
 // caller-provided workspace. kNoAllocScratchFloats floats (4 MiB) on every GPU
 // that loads the library, held until the process exits. Host code cannot use
-// the array's name as a device address; noalloc_scratch() resolves it.
+// the array's name as a device address (it names a host-side stand-in);
+// noalloc_scratch() resolves the device address.
 static __device__ __align__(256) float g_noalloc_scratch[kNoAllocScratchFloats];
 
-// Device address of g_noalloc_scratch on the current device: looked up once
-// per device, with that device current, and cached.
+// Device address of g_noalloc_scratch in the calling thread's current
+// context, resolved on every call. Once the library's module is loaded in a
+// context the lookup is a host-side table read (the first call in a context
+// loads the module there). An address kept from an earlier call could be
+// stale: after cudaDeviceReset the module is loaded again in a new primary
+// context, and a caller that makes another driver context current on the
+// same device sees that context's copy of the array; a kernel given the old
+// address would write through it.
 cudaError_t noalloc_scratch(float** out) {
-  static std::mutex mu;
-  static float* addr[kMaxScratchDevices] = {};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
   if (e != cudaSuccess) return e;
-  if (dev < 0 || dev >= kMaxScratchDevices) return cudaErrorInvalidDevice;
-  std::lock_guard<std::mutex> lock(mu);
-  if (addr[dev] == nullptr) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_noalloc_scratch);
-    if (e != cudaSuccess) return e;
-    addr[dev] = static_cast<float*>(p);
-  }
-  *out = addr[dev];
+  *out = static_cast<float*>(p);
   return cudaSuccess;
 }
 
@@ -370,7 +366,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 256 ? 2 : 1)
   int64_t row = blockIdx.x;
   for (int64_t k = 0; k < nrows; ++k, row += G) {
     const uint32_t base = ring + (uint32_t)s * stage_bytes;
-    int bad = mbar_wait_bounded(smem_addr(&full_bar[s]), use & 1u, kWaitLimitCycles) ? 0 : 1;
+    int bad = mbar_wait_bounded(smem_addr(&full_bar[s]), use & 1u, qa.wait_limit) ? 0 : 1;
     // (sum r^2, sum dt * r) in the order of the kernel above
     float2 sq = make_float2(0.0f, 0.0f), pr = make_float2(0.0f, 0.0f);
 #pragma unroll

@@ -18,6 +18,10 @@ namespace {
 
 thread_local char g_err[512] = "";
 
+// Limit (SM cycles) on every wait of the kernels this thread launches; set
+// through cutie_set_wait_limit, kWaitLimitCycles by default.
+thread_local long long g_wait_limit = kWaitLimitCycles;
+
 int fail(int code, const char* fmt, ...) {
   va_list ap;
   va_start(ap, fmt);
@@ -440,6 +444,7 @@ int run_fused(bool norm, const void* x, int64_t ldx, const void* residual, int64
   a.scale_fmt = scale_fmt;
   a.scale_layout = swz ? kLaySwizzled : kLayStrided;
   a.stages = 0;
+  a.wait_limit = g_wait_limit;
 
   const bool res = residual != nullptr;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -617,6 +622,7 @@ int prepare_backward(const void* d_normalized, int64_t ldd, const void* r, int64
   qa.n_groups_pad = (int)n_groups_pad;
   qa.scale_fmt = scale_fmt;
   qa.scale_layout = swz ? kLaySwizzled : kLayStrided;
+  qa.wait_limit = g_wait_limit;
   return CUTIE_OK;
 }
 
@@ -701,6 +707,12 @@ extern "C" int cutie_device_error(int clear) {
     if (any == 0) any = v;
   }
   return any;
+}
+
+extern "C" int64_t cutie_set_wait_limit(int64_t cycles) {
+  const long long prev = g_wait_limit;
+  g_wait_limit = cycles == 0 ? kWaitLimitCycles : (long long)cycles;
+  return prev;
 }
 
 extern "C" const char* cutie_last_error(void) { return g_err; }

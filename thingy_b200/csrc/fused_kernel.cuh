@@ -73,6 +73,7 @@ struct FusedArgs {
   int scale_fmt;
   int scale_layout;
   int stages;           // shared-memory ring depth (>= 2)
+  long long wait_limit; // SM cycles a wait may block before it gives up (< 0: never blocks)
 };
 
 // ---------------------------------------------------------------- bit helpers
@@ -298,14 +299,30 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return done != 0;
 }
 
-// Wait for phase `parity` of an mbarrier, giving up after `limit` cycles.
+// Non-blocking: has phase `parity` of the mbarrier completed?
+__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
+  uint32_t done;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      " selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(done)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return done != 0;
+}
+
+// Wait for phase `parity` of an mbarrier: one non-blocking test (the phase
+// has usually completed), then suspending try_waits while fewer than `limit`
+// SM cycles have passed. limit < 0 never blocks: the wait gives up as soon as
+// the test finds the phase incomplete (the failure path can be exercised with
+// copies that are valid and still land).
 __device__ __forceinline__ bool mbar_wait_bounded(uint32_t bar, uint32_t parity,
                                                   long long limit) {
-  if (mbar_try_wait(bar, parity)) return true;
+  if (mbar_test(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity))
-    if (clock64() - t0 > limit) return false;
-  return true;
+  while (clock64() - t0 <= limit)
+    if (mbar_try_wait(bar, parity)) return true;
+  return false;
 }
 
 // Global -> shared bulk copy (no multicast), completion counted on `bar`.
@@ -319,7 +336,7 @@ __device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t
       : "memory");
 }
 
-constexpr long long kWaitLimitCycles = 4000000000LL;  // ~2 s at the B200's clocks
+constexpr long long kWaitLimitCycles = 4000000000LL;  // default limit: ~2 s at the B200's clocks
 constexpr long long kDrainLimitCycles = 400000000LL;  // per stage, after an error
 
 // ------------------------------------------------------------ arithmetic
@@ -577,7 +594,7 @@ __global__ void __launch_bounds__(NCH == 1 ? 1024 : 512) fused_rmsnorm_fp8_kerne
     }
     const uint32_t bar = bars + 8u * (uint32_t)s;
     const uint32_t base = ring + (uint32_t)s * stage_bytes;
-    int bad = mbar_wait_bounded(bar, parity, kWaitLimitCycles) ? 0 : 1;
+    int bad = mbar_wait_bounded(bar, parity, a.wait_limit) ? 0 : 1;
 
     uint32_t v[NV][4];
 #pragma unroll
@@ -913,7 +930,7 @@ __global__ void __launch_bounds__(kRowwarpWarps * 32, RES ? 6 : 8)
   uint32_t pos_par = 0;
   auto take = [&](uint32_t (&x)[4][4], uint32_t (&r)[4][4], int piece) -> bool {
     const uint32_t slot = (uint32_t)pos_slot;
-    const bool ok = mbar_wait_bounded(bars + 8u * slot, pos_par, kWaitLimitCycles);
+    const bool ok = mbar_wait_bounded(bars + 8u * slot, pos_par, a.wait_limit);
     const uint32_t base = ring + slot * kSlot;
     const int c = piece * 32 + lane;  // chunk index in the row
 #pragma unroll

@@ -213,10 +213,9 @@ struct BwdArgs {
 // of dw partial sums the workspace holds).
 void backward_shape(int64_t M, int64_t H, int* threads, int* grid);
 // Floats of the d_weight scratch the allocation-free backward keeps in a
-// device array of the library (backward.cu), and that array's address on the
-// current device (resolved once per device).
+// device array of the library (backward.cu), and that array's address in the
+// current context (resolved on every call).
 constexpr int64_t kNoAllocScratchFloats = int64_t(1) << 20;
-constexpr int kMaxScratchDevices = 64;
 cudaError_t noalloc_scratch(float** out);
 
 // Device error word of backward.cu (see read_device_error).

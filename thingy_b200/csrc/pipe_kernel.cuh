@@ -26,9 +26,10 @@
 //
 // A warp can run up to about three rows ahead of the slowest one, which is
 // why the rings are four deep (the argument is spelled out at the rings).
-// Waits are bounded (about 2 s): a wait that gives up sets the device error
-// word and an abort flag that ends every other wait of the CTA, and the CTA
-// lets every copy it issued land (bounded) before it exits.
+// Waits are bounded (FusedArgs::wait_limit, about 2 s by default): a wait
+// that gives up sets the device error word and an abort flag that ends every
+// other wait of the CTA, no stage is refilled after that, and the CTA lets
+// the last copy it issued into each stage land (bounded) before it exits.
 //
 // Arithmetic shared with the single-pass kernel lives in fused_kernel.cuh;
 // the two sm_90+ forms used only here are the mixed-precision square
@@ -56,32 +57,19 @@ __device__ __forceinline__ void mbar_arrive(uint32_t bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
 }
 
-__device__ __forceinline__ bool mbar_test(uint32_t bar, uint32_t parity) {
-  uint32_t done;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n"
-      " selp.u32 %0, 1, 0, p;\n}"
-      : "=r"(done)
-      : "r"(bar), "r"(parity)
-      : "memory");
-  return done != 0;
-}
-
-// Wait for phase `parity`: one non-blocking test first (the phase has
-// usually completed), then suspending try_waits, giving up after
-// kWaitLimitCycles or at once when the CTA's abort flag is set. A wait that
+// Wait for phase `parity` as mbar_wait_bounded does (one non-blocking test,
+// then suspending try_waits for at most `limit` cycles; limit < 0 never
+// blocks), giving up at once when the CTA's abort flag is set. A wait that
 // gives up sets the flag, so every later wait of the CTA returns at once.
 __device__ __forceinline__ bool mbar_wait_abortable(uint32_t bar, uint32_t parity,
-                                                    volatile uint32_t* abort_flag) {
+                                                    volatile uint32_t* abort_flag,
+                                                    long long limit) {
   if (mbar_test(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*abort_flag || clock64() - t0 > kWaitLimitCycles) {
-      *abort_flag = 1u;
-      return false;
-    }
-  }
-  return true;
+  while (!*abort_flag && clock64() - t0 <= limit)
+    if (mbar_try_wait(bar, parity)) return true;
+  *abort_flag = 1u;
+  return false;
 }
 
 // Streaming fp32 store guarded by `ok` inside the instruction (no branch).
@@ -308,7 +296,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   // ---------------------------------------------------------------- phase A
   auto phase_a = [&](int k, int s, uint32_t par, uint8_t* rorow) {
     const uint32_t base = ring + (uint32_t)s * stage_bytes;
-    ok &= mbar_wait_abortable(smem_addr(&full_bar[s]), par, abortp);
+    ok &= mbar_wait_abortable(smem_addr(&full_bar[s]), par, abortp, a.wait_limit);
     uint32_t v[NV][4];
 #pragma unroll
     for (int k2 = 0; k2 < NV; ++k2) {
@@ -365,7 +353,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
   auto finalize = [&](int k) {
     const int slot = k & (kPipeRing - 1);
     const uint32_t par = (uint32_t)(k >> 2) & 1u;
-    ok &= mbar_wait_abortable(smem_addr(&red_bar[slot]), par, abortp);
+    ok &= mbar_wait_abortable(smem_addr(&red_bar[slot]), par, abortp, a.wait_limit);
     const float total = combine_partials<false>(part[slot], lane, nw);
     float mean = div_rn(total, (float)a.H, a.rcp_H);
     if (mean < 0x1p-100f) mean = __fdiv_rn(total, (float)a.H);
@@ -396,10 +384,14 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
     // Count this warp out of the stage; the last warp refills it. The
     // acq_rel add orders every lane's reads (joined by __syncwarp) before the
     // refill, and the proxy fence orders them before the copy engine's writes.
+    // No refill once the CTA is aborting: a warp whose wait for this stage's
+    // copy gave up set the abort flag before it counted out, so the last warp
+    // sees the flag, and the copy that may still be landing in the stage is
+    // the only one there when the CTA drains.
     __syncwarp();
     if (lane == 0) {
       const uint32_t old = atom_add_acq_rel(smem_addr(&done_cnt[s]), 1u);
-      if (old + 1u == (use + 1u) * (uint32_t)nw && k + S < nrows) {
+      if (old + 1u == (use + 1u) * (uint32_t)nw && k + S < nrows && !*abortp) {
         fence_proxy_async_smem();
         issued_cnt[s] = use + 2u;
         issue(s, row + (int64_t)S * G);
@@ -415,7 +407,7 @@ __global__ void __launch_bounds__(MAXT, MAXT <= 224 ? 4 : 1)
       w[k2][2] = u.z;
       w[k2][3] = u.w;
     }
-    ok &= mbar_wait_abortable(smem_addr(&inv_bar[slot]), par, abortp);
+    ok &= mbar_wait_abortable(smem_addr(&inv_bar[slot]), par, abortp, a.wait_limit);
     const float inv = inv_slot[slot];
     const float2 inv2 = make_float2(inv, inv);
     {

@@ -17,10 +17,24 @@ import torch
 
 from . import _lib
 
-try:
-    from . import _C as _binding
-except ImportError:  # the ctypes path below covers the same entry points
-    _binding = None
+_UNSET = object()
+_binding_mod = _UNSET
+
+
+def _binding():
+    """The torch binding, imported on first use (None if it was not built).
+
+    Importing it maps libcutie_b200.so too, so it is deferred until an op
+    runs: importing the package (or a pure-Python submodule such as
+    ``workloads``) loads no native code."""
+    global _binding_mod
+    if _binding_mod is _UNSET:
+        try:
+            from . import _C as mod
+        except ImportError:  # the ctypes path below covers the same entry points
+            mod = None
+        _binding_mod = mod
+    return _binding_mod
 from .layouts import SCALE_FORMATS, SCALE_LAYOUTS, mx_swizzled_size, n_groups
 
 _FMT_CODE = {"fp32": _lib.SCALE_FP32, "ue8m0": _lib.SCALE_FP32_POW2, "e8m0": _lib.SCALE_E8M0}
@@ -164,17 +178,18 @@ def launch_rms_norm_fp8(
         raise ValueError(f"scale_format must be one of {SCALE_FORMATS}")
     if scale_layout not in SCALE_LAYOUTS:
         raise ValueError(f"scale_layout must be one of {SCALE_LAYOUTS}")
-    if _binding is not None and not isinstance(stream, int):
+    binding = _binding() if not isinstance(stream, int) else None
+    if binding is not None:
         if not isinstance(x, torch.Tensor):
             raise TypeError("x must be a torch.Tensor")
         args = (x, weight, float(eps), residual, q, scale, residual_out, normalized_out,
                 int(group_size or 0), _FMT_CODE[scale_format], _LAYOUT_CODE[scale_layout],
                 int(threads_per_row), bool(normalize))
         if stream is None:
-            _binding.rms_norm_fp8(*args)
+            binding.rms_norm_fp8(*args)
         else:
             with torch.cuda.stream(stream):
-                _binding.rms_norm_fp8(*args)
+                binding.rms_norm_fp8(*args)
         return
     M, H = _check_x(x)
     device = x.device
@@ -240,12 +255,13 @@ def launch_rms_norm(
     stream=None,
 ) -> None:
     """Enqueue a standalone RMSNorm (bf16 or fp32, see include/cutie.h)."""
-    if _binding is not None and not isinstance(stream, int):
+    binding = _binding() if not isinstance(stream, int) else None
+    if binding is not None:
         if stream is None:
-            _binding.rms_norm(x, weight, float(eps), out, int(threads_per_row))
+            binding.rms_norm(x, weight, float(eps), out, int(threads_per_row))
         else:
             with torch.cuda.stream(stream):
-                _binding.rms_norm(x, weight, float(eps), out, int(threads_per_row))
+                binding.rms_norm(x, weight, float(eps), out, int(threads_per_row))
         return
     if x.dtype not in (torch.bfloat16, torch.float32):
         raise ValueError(f"x must be bfloat16 or float32, got {x.dtype}")

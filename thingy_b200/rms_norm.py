@@ -6,6 +6,12 @@ residual_out, normalized_out, stream)`` (rms_norm.py:36-113), but launches the
 hand-written sm_100a kernel through the C ABI instead of a CuTe DSL JIT.
 ``rms_norm`` / ``rms_norm_on_stream`` replace the torch.compile baseline
 (rms_norm.py:11-33); ``out`` is honoured here (the reference ignores it).
+The reference's ``rms_norm`` is itself a torch.compile region; here it is
+backed by two torch.library ops with fake implementations,
+``thingy_b200::rms_norm`` (functional) and ``thingy_b200::rms_norm_out``
+(writes ``out``), so ``torch.compile(fullgraph=True)`` traces a call to
+``rms_norm`` as one opaque op. Eager calls skip the op dispatcher and launch
+through the binding directly.
 """
 
 from __future__ import annotations
@@ -93,6 +99,35 @@ class RMSNorm:
         )
 
 
+def _rms_norm_into(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor) -> None:
+    H = x.shape[-1]
+    x2 = x if x.dim() == 2 else x.reshape(-1, H)
+    out2 = out if out.dim() == 2 else out.view(-1, H)
+    launch_rms_norm(x2, weight, eps, out2)
+
+
+@torch.library.custom_op("thingy_b200::rms_norm", mutates_args=())
+def rms_norm_op(x: torch.Tensor, weight: torch.Tensor, eps: float) -> torch.Tensor:
+    out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    _rms_norm_into(x, weight, eps, out)
+    return out
+
+
+@rms_norm_op.register_fake
+def _rms_norm_op_fake(x, weight, eps):
+    return torch.empty_like(x, memory_format=torch.contiguous_format)
+
+
+@torch.library.custom_op("thingy_b200::rms_norm_out", mutates_args=("out",))
+def rms_norm_out_op(x: torch.Tensor, weight: torch.Tensor, eps: float, out: torch.Tensor) -> None:
+    _rms_norm_into(x, weight, eps, out)
+
+
+@rms_norm_out_op.register_fake
+def _rms_norm_out_op_fake(x, weight, eps, out):
+    return None
+
+
 def rms_norm(
     x: torch.Tensor,
     weight: torch.Tensor,
@@ -104,14 +139,18 @@ def rms_norm(
     fp32 x: ``x / sqrt(mean(x^2) + eps) * weight`` in fp32 (rms_norm.py:11-20).
     bf16 x: ``bf16(x * rsqrt(mean(x^2) + eps)) * weight`` with fp32 statistics
     (the Prime-RL form at bench.py:58-65 that the fused path generalises).
+    Inside a torch.compile region the call is the op ``thingy_b200::rms_norm``
+    (or ``thingy_b200::rms_norm_out`` when ``out`` is given).
     """
-    H = x.shape[-1]
-    x2 = x if x.dim() == 2 else x.reshape(-1, H)
+    if torch.compiler.is_compiling():
+        if out is None:
+            return torch.ops.thingy_b200.rms_norm(x, weight, float(eps))
+        torch.ops.thingy_b200.rms_norm_out(x, weight, float(eps), out)
+        return out
     if out is None:
-        out = torch.empty_like(x2)
-    out2 = out if out.dim() == 2 else out.reshape(-1, H)
-    launch_rms_norm(x2, weight, eps, out2)
-    return out.reshape(x.shape)
+        out = torch.empty_like(x, memory_format=torch.contiguous_format)
+    _rms_norm_into(x, weight, eps, out)
+    return out
 
 
 def rms_norm_on_stream(
