@@ -59,6 +59,9 @@ def _kernel_name(w, threads_per_row) -> str:
         return "rmsnorm_backward_ring_kernel" if w.H <= 16384 else "rmsnorm_backward_kernel"
     if threads_per_row == 32:
         return "rowwarp_rmsnorm_fp8_kernel"
+    if (not threads_per_row and not w.residual and w.M >= 4096 and w.H <= 8192
+            and w.group_size in (None, 128)):
+        return "rowstage_rmsnorm_fp8_kernel"  # one warp a row, the row in registers
     if w.group_size is None:  # per-token scaling: the single-pass kernel
         return "fused_rmsnorm_fp8_kernel"
     return "pipe_rmsnorm_fp8_kernel"

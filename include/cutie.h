@@ -227,6 +227,23 @@ CUTIE_API int cutie_rms_norm_backward_noalloc(const void* d_normalized, int64_t 
                                               void* q, int64_t ldq, void* scale, void* stream);
 
 /*
+ * MXFP8 block-scaled GEMM on the tensor cores, the consumer of this path's
+ * 1x32 codes and swizzled e8m0 scales (no counterpart in the reference, whose
+ * bench stops before the GEMM, src/cutie/rms_norm/bench.py:4-7):
+ *   D[m, n] = bf16( sum_k A[m, k] 2^(sA[m, k/32] - 127) * B[n, k] 2^(sB[n, k/32] - 127) )
+ * with fp32 accumulation. a: e4m3 [M, K] (K contiguous, lda bytes between
+ * rows), a_scale: its e8m0 scales in CUTIE_LAYOUT_MX_SWIZZLED for [M, K/32]
+ * (rows padded to 128, as cutie_rms_norm_fp8 writes them); b: e4m3 [N, K]
+ * (ldb) with b_scale likewise for [N, K/32]; d: bf16 [M, N] (ldd elements).
+ * N and K multiples of 128, any M >= 0; a, b, d rows and both scale buffers
+ * 16-byte aligned. Asynchronous on `stream`; nothing is allocated.
+ */
+CUTIE_API int cutie_gemm_mxfp8(const void* a, int64_t lda, const void* a_scale,
+                               const void* b, int64_t ldb, const void* b_scale,
+                               void* d, int64_t ldd, int64_t M, int64_t N, int64_t K,
+                               void* stream);
+
+/*
  * Device-side status of this library's kernels on the current device: 0 when
  * no kernel has hit a failure since the last clear; otherwise the first error
  * code recorded (1 = a bulk-copy wait ran out: a row never arrived in shared

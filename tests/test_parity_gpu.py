@@ -63,6 +63,34 @@ def test_bulk_path_bitexact(group_size, fmt, layout, residual, M, H):
     check_parity(inp, group_size, fmt, layout, exact=True)
 
 
+ROWSTAGE_MODES = [
+    (None, "fp32", "row"), (None, "ue8m0", "col"), (128, "fp32", "col"), (128, "ue8m0", "row"),
+    (128, "e8m0", "row"), (128, "e8m0", "packed"), (128, "e8m0", "mx"),
+]
+
+
+@pytest.mark.parametrize("group_size,fmt,layout", ROWSTAGE_MODES)
+@pytest.mark.parametrize("M,H", [(4096, 1000), (4100, 8184), (4500, 7168), (4097, 2056),
+                                 (4099, 5120)])
+def test_row_staged_bitexact(group_size, fmt, layout, M, H):
+    """Residual-free batches of >= 4096 rows up to 8192 columns go to the
+    row-staged kernel (one warp a row, the row held in registers) for 1x128
+    groups and per-token scales, every scale destination: row widths from
+    one 2 KB block to eight, whole and ragged last blocks, rows not a
+    multiple of the warps."""
+    inp = exact_sum_inputs(M, H, residual=False, seed=M * 11 + H)
+    check_parity(inp, group_size, fmt, layout, exact=True)
+
+
+@pytest.mark.parametrize("M,H", [(4096, 4096), (4111, 1032), (5000, 8192)])
+def test_row_staged_plain_rmsnorm(M, H):
+    """The row-staged kernel's no-quantization mode (bf16 RMSNorm output)."""
+    inp = exact_sum_inputs(M, H, residual=False, seed=M + 3 * H)
+    y = tb.rms_norm(inp["x"].cuda(), inp["weight"].cuda(), 1e-6)
+    ref = ora.rms_norm_reference(inp["x"], inp["weight"], 1e-6)
+    np.testing.assert_array_equal(bf16_bits(y), bf16_bits(ref))
+
+
 @pytest.mark.parametrize("group_size,fmt,layout", MODES)
 @pytest.mark.parametrize("residual", [False, True])
 @pytest.mark.parametrize("M,H", [(3, 7168), (41, 8192), (70, 1000), (9, 200), (5, 16384),

@@ -35,6 +35,7 @@ EXPORTED_SYMBOLS = (
     "cutie_rms_norm_backward",
     "cutie_rms_norm_backward_workspace",
     "cutie_rms_norm_backward_noalloc",
+    "cutie_gemm_mxfp8",
     "cutie_device_error",
     "cutie_set_wait_limit",
     "cutie_last_error",
@@ -70,6 +71,9 @@ _SIGNATURES = {
         _int,
         [_ptr, _i64, _ptr, _i64, _ptr, _ptr, _i64, _f32, _i64, _i64, _ptr, _i64, _ptr,
          _int, _int, _int, _int, _i64, _ptr, _i64, _ptr, _ptr],
+    ),
+    "cutie_gemm_mxfp8": (
+        _int, [_ptr, _i64, _ptr, _ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, _i64, _ptr],
     ),
     "cutie_device_error": (_int, [_int]),
     "cutie_set_wait_limit": (_i64, [_i64]),

@@ -198,6 +198,38 @@ BulkPlan plan_pipe(const void* kernel, int threads, int stage_bytes) {
   return plan;
 }
 
+RowstagePlan plan_rowstage(const void* kernel, int row_pad, int max_warps) {
+  static std::mutex mu;
+  static std::unordered_map<uint64_t, RowstagePlan> cache;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  const uint64_t key = (reinterpret_cast<uint64_t>(kernel) * 0x9E3779B97F4A7C15ull) ^
+                       (static_cast<uint64_t>(row_pad) << 12) ^ static_cast<uint64_t>(dev);
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    auto it = cache.find(key);
+    if (it != cache.end()) return it->second;
+  }
+  RowstagePlan plan{0, 0};
+  int block_smem = 0;
+  cudaFuncAttributes attr{};
+  if (cudaDeviceGetAttribute(&block_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) !=
+          cudaSuccess ||
+      cudaFuncGetAttributes(&attr, kernel) != cudaSuccess)
+    return plan;
+  // one slot a warp plus the weights' slot, as many warps as fit (and as the
+  // kernel's register budget allows)
+  int warps = (block_smem - (int)attr.sharedSizeBytes) / row_pad - 1;
+  if (warps > max_warps) warps = max_warps;
+  if (warps >= kRowstageMinWarps) {
+    plan = RowstagePlan{warps, (warps + 1) * row_pad};
+    if (set_smem_and_occupancy(kernel, warps * 32, plan.smem_bytes) <= 0) plan = RowstagePlan{0, 0};
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  cache[key] = plan;
+  return plan;
+}
+
 namespace {
 
 
@@ -234,12 +266,12 @@ int pick_shape(int64_t V, int64_t M, int requested, bool aliased, LaunchShape* o
   int64_t T = (NC + 31) / 32 * 32;
   if (T < 32) T = 32;
   if (T <= 1024) {
-    *out = {1, (int)T, false, true};
+    *out = {1, (int)T, false, true, true};
     return CUTIE_OK;
   }
   T = ((NC + 1) / 2 + 31) / 32 * 32;
   if (T <= 512) {
-    *out = {2, (int)T, false, false};
+    *out = {2, (int)T, false, false, true};
     return CUTIE_OK;
   }
   if (!aliased) {  // wider rows than one CTA can hold: stream them per warp
@@ -694,12 +726,40 @@ extern "C" int cutie_rms_norm_backward_noalloc(const void* d_normalized, int64_t
   return CUTIE_OK;
 }
 
+extern "C" int cutie_gemm_mxfp8(const void* a, int64_t lda, const void* a_scale, const void* b,
+                                int64_t ldb, const void* b_scale, void* d, int64_t ldd,
+                                int64_t M, int64_t N, int64_t K, void* stream) {
+  g_err[0] = '\0';
+  if (M < 0 || N <= 0 || K <= 0)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "need M >= 0, N > 0 and K > 0 (got %lld, %lld, %lld)",
+                (long long)M, (long long)N, (long long)K);
+  if (N % 128 != 0 || K % 128 != 0)
+    return fail(CUTIE_ERR_UNSUPPORTED, "N and K must be multiples of 128 (got N=%lld, K=%lld)",
+                (long long)N, (long long)K);
+  if (M > INT32_MAX || N > INT32_MAX || K > INT32_MAX)
+    return fail(CUTIE_ERR_UNSUPPORTED, "M, N and K must be below 2^31");
+  if (M == 0) return CUTIE_OK;
+  int rc;
+  if ((rc = check_matrix("a", a, lda, K, 16, 16)) != CUTIE_OK) return rc;
+  if ((rc = check_matrix("b", b, ldb, K, 16, 16)) != CUTIE_OK) return rc;
+  if ((rc = check_matrix("d", d, ldd, N, 16, 8)) != CUTIE_OK) return rc;
+  if (a_scale == nullptr || b_scale == nullptr)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "a_scale and b_scale must not be NULL");
+  if (!aligned(a_scale, 16) || !aligned(b_scale, 16))
+    return fail(CUTIE_ERR_ALIGNMENT, "the swizzled scale buffers must be 16-byte aligned");
+  const char* why = "";
+  rc = gemm_mxfp8(a, lda, a_scale, b, ldb, b_scale, d, ldd, M, N, K,
+                  static_cast<cudaStream_t>(stream), &why);
+  if (rc != CUTIE_OK) return fail(rc, "mxfp8 gemm: %s", why);
+  return CUTIE_OK;
+}
+
 extern "C" int cutie_device_error(int clear) {
   g_err[0] = '\0';
   int any = 0;
   cudaError_t (*readers[])(int*, bool) = {device_error_none, device_error_token, device_error_g32,
                                           device_error_g64, device_error_g128,
-                                          device_error_bwd};
+                                          device_error_bwd,  device_error_gemm};
   for (auto read : readers) {
     int v = 0;
     const cudaError_t e = read(&v, clear != 0);

@@ -1104,10 +1104,11 @@ __global__ void __launch_bounds__(kRowwarpWarps * 32, RES ? 6 : 8)
 
 // Host-side launch shape.
 struct LaunchShape {
-  int nch;      // single-pass kernel: 64-byte chunks per thread, 1 or 2
-  int threads;  // single-pass kernel: threads per CTA (one row at a time)
-  bool rowwarp; // use the warp-per-row two-pass kernel instead
-  bool pipe;    // nch == 1: prefer the pipelined kernel (pipe_kernel.cuh) where it applies
+  int nch;        // single-pass kernel: 64-byte chunks per thread, 1 or 2
+  int threads;    // single-pass kernel: threads per CTA (one row at a time)
+  bool rowwarp;   // use the warp-per-row two-pass kernel instead
+  bool pipe;      // nch == 1: prefer the pipelined kernel (pipe_kernel.cuh) where it applies
+  bool rowstage;  // automatic shape: prefer the row-staged kernel (rowstage_kernel.cuh)
 };
 
 }  // namespace cutie

@@ -5,6 +5,7 @@
 
 #include "fused_kernel.cuh"
 #include "pipe_kernel.cuh"
+#include "rowstage_kernel.cuh"
 
 namespace cutie {
 
@@ -131,8 +132,77 @@ cudaError_t launch_pipe(const FusedArgs& a, int threads, cudaStream_t stream, bo
   }
 }
 
+// Plan of the row-staged kernel: one CTA an SM of `warps` warps, each with
+// one row slot of `row_pad` bytes, plus one slot for the weights. warps == 0:
+// no plan (fewer than kRowstageMinWarps fit in one CTA's shared memory).
+struct RowstagePlan {
+  int warps;
+  int smem_bytes;
+};
+constexpr int kRowstageMinWarps = 4;
+// Batches of fewer rows keep the CTA-per-row kernels: with about one row a
+// warp the row-staged kernel cannot hide its per-row latency (measured on a
+// B200 at H = 7168: 2048 rows 14.8 vs 13.9 us, 4096 rows 21.6 vs 21.9 us).
+constexpr int64_t kRowstageMinRows = 4096;
+RowstagePlan plan_rowstage(const void* kernel, int row_pad, int max_warps);
+
+template <int QM, int NB, int SK>
+cudaError_t launch_rowstage_one(FusedArgs a, cudaStream_t stream, bool* launched) {
+  auto kernel = rowstage_rmsnorm_fp8_kernel<QM, NB, SK>;
+  const RowstagePlan p = plan_rowstage(reinterpret_cast<const void*>(kernel),
+                                       NB * (int)kRowstageBlockBytes, rowstage_max_warps(NB));
+  *launched = false;
+  if (p.warps < kRowstageMinWarps) return cudaSuccess;
+  int64_t grid = device_sm_count();
+  const int64_t need = (a.M + p.warps - 1) / p.warps;
+  if (grid > need) grid = need;
+  *launched = true;
+  if (grid <= 0) return cudaSuccess;
+  return launch_pdl(kernel, (unsigned)grid, (unsigned)(p.warps * 32), (size_t)p.smem_bytes,
+                    stream, a);
+}
+
+template <int QM, int SK>
+cudaError_t launch_rowstage_sk(const FusedArgs& a, cudaStream_t stream, bool* launched) {
+  switch ((a.V + 127) / 128) {
+    case 1: return launch_rowstage_one<QM, 1, SK>(a, stream, launched);
+    case 2: return launch_rowstage_one<QM, 2, SK>(a, stream, launched);
+    case 3: return launch_rowstage_one<QM, 3, SK>(a, stream, launched);
+    case 4: return launch_rowstage_one<QM, 4, SK>(a, stream, launched);
+    case 5: return launch_rowstage_one<QM, 5, SK>(a, stream, launched);
+    case 6: return launch_rowstage_one<QM, 6, SK>(a, stream, launched);
+    case 7: return launch_rowstage_one<QM, 7, SK>(a, stream, launched);
+    case 8: return launch_rowstage_one<QM, 8, SK>(a, stream, launched);
+    default: *launched = false; return cudaSuccess;  // wider rows: the other kernels
+  }
+}
+
+template <int QM>
+cudaError_t launch_rowstage(const FusedArgs& a, cudaStream_t stream, bool* launched) {
+  if constexpr (QM == kQNone) {
+    return launch_rowstage_sk<QM, kSkF32>(a, stream, launched);
+  } else {
+    if (QM == kQGroup && a.scale_layout == kLaySwizzled)
+      return launch_rowstage_sk<QM, kSkE8Swz>(a, stream, launched);
+    switch (a.scale_fmt) {
+      case kFmtE8M0: return launch_rowstage_sk<QM, kSkE8>(a, stream, launched);
+      case kFmtPow2: return launch_rowstage_sk<QM, kSkF32Pow2>(a, stream, launched);
+      default: return launch_rowstage_sk<QM, kSkF32>(a, stream, launched);
+    }
+  }
+}
+
 template <int QM, int LPG, bool RES, bool NORM>
 cudaError_t launch_fused_nch(const FusedArgs& a, LaunchShape sh, cudaStream_t stream) {
+  // Residual-free batches of many rows: the row-staged kernel (1x128 groups,
+  // one scale a row, or no quantization).
+  if constexpr (NORM && !RES && (QM == kQToken || QM == kQNone || (QM == kQGroup && LPG == 4))) {
+    if (sh.rowstage && a.M >= kRowstageMinRows) {
+      bool launched = false;
+      const cudaError_t e = launch_rowstage<QM>(a, stream, &launched);
+      if (e != cudaSuccess || launched) return e;
+    }
+  }
   if constexpr (NORM && QM != kQToken) {
     if (sh.pipe) {
       bool launched = false;
@@ -220,6 +290,13 @@ cudaError_t noalloc_scratch(float** out);
 
 // Device error word of backward.cu (see read_device_error).
 cudaError_t device_error_bwd(int* out, bool clear);
+
+// MXFP8 block-scaled GEMM (gemm_mxfp8.cu): arguments checked by the caller;
+// returns a CUTIE_* status and, on failure, points *why at a message.
+int gemm_mxfp8(const void* a, int64_t lda, const void* a_scale, const void* b, int64_t ldb,
+               const void* b_scale, void* d, int64_t ldd, int64_t M, int64_t N, int64_t K,
+               cudaStream_t stream, const char** why);
+cudaError_t device_error_gemm(int* out, bool clear);
 
 // max_grid > 0 caps the CTAs (and so the rows of partial sums in a.partial).
 cudaError_t launch_backward(const BwdArgs& a, float eps, bool dw_wanted, uint16_t* dw,

@@ -1,0 +1,62 @@
+"""The downstream consumer of the path's MXFP8 output: a block-scaled FP8 GEMM.
+
+``mxfp8_gemm(a, a_scale, b, b_scale)`` multiplies e4m3 codes with 1x32 e8m0
+scales in the Blackwell swizzled layout (what ``rms_norm_fp8(...,
+group_size=32, scale_format="e8m0", scale_layout="mx")`` returns) by a weight
+quantized the same way, on the tensor cores (``cutie_gemm_mxfp8``,
+hand-written tcgen05 kernel), fp32 accumulation, bf16 out:
+``D = dequant(a) @ dequant(b).T``. The reference has no GEMM on this path
+(src/cutie/rms_norm/bench.py stops before it); this is the consumer its
+quantizer feeds.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from . import _lib
+from .layouts import mx_swizzled_size
+from .ops import E8M0_DTYPES, FP8_DTYPE
+
+
+def _operand(name: str, t: torch.Tensor, K: int) -> int:
+    if not isinstance(t, torch.Tensor) or t.dim() != 2 or not t.is_cuda:
+        raise ValueError(f"{name} must be a 2-D CUDA tensor")
+    if t.dtype not in (FP8_DTYPE, torch.uint8):
+        raise ValueError(f"{name} must be float8_e4m3fn, got {t.dtype}")
+    if t.shape[1] != K or (t.shape[0] > 1 and t.stride(1) != 1):
+        raise ValueError(f"{name} must be [rows, {K}] and contiguous along K")
+    return max(t.stride(0), K) if t.shape[0] > 1 else K
+
+
+def mxfp8_gemm(a: torch.Tensor, a_scale: torch.Tensor, b: torch.Tensor, b_scale: torch.Tensor,
+               out: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 [M, N] = (a * 2^(a_scale-127)) @ (b * 2^(b_scale-127)).T, on the current stream.
+
+    a: e4m3 [M, K]; b: e4m3 [N, K]; a_scale / b_scale: e8m0 scales of 1x32
+    groups in the swizzled layout ([rows padded to 128] x [K/32 padded to 4]
+    bytes). N and K must be multiples of 128.
+    """
+    M, K = a.shape
+    N = b.shape[0]
+    lda, ldb = _operand("a", a, K), _operand("b", b, K)
+    for name, s, rows in (("a_scale", a_scale, M), ("b_scale", b_scale, N)):
+        if s.dtype not in E8M0_DTYPES or not s.is_contiguous() or s.device != a.device:
+            raise ValueError(f"{name} must be contiguous e8m0 (or uint8) bytes on {a.device}")
+        if s.numel() < mx_swizzled_size(rows, -(-K // 32)):
+            raise ValueError(f"{name} holds {s.numel()} bytes, the swizzled layout needs "
+                             f"{mx_swizzled_size(rows, -(-K // 32))}")
+    if b.device != a.device:
+        raise ValueError("a and b must be on the same device")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=a.device)
+    elif out.shape != (M, N) or out.dtype != torch.bfloat16 or (N > 1 and out.stride(1) != 1):
+        raise ValueError(f"out must be a bf16 [{M}, {N}] tensor contiguous along N")
+    ldd = max(out.stride(0), N) if M > 1 else N
+    lib = _lib.load()
+    with torch.cuda.device(a.device):
+        status = lib.cutie_gemm_mxfp8(
+            a.data_ptr(), lda, a_scale.data_ptr(), b.data_ptr(), ldb, b_scale.data_ptr(),
+            out.data_ptr(), ldd, M, N, K, torch.cuda.current_stream(a.device).cuda_stream)
+    _lib.check(status)
+    return out
