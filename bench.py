@@ -57,6 +57,8 @@ def _kernel_name(w, threads_per_row) -> str:
         return "rmsnorm_f32_kernel"
     if w.kind == "bwd":  # rows of up to 16384 take the bulk-copy ring variant
         return "rmsnorm_backward_ring_kernel" if w.H <= 16384 else "rmsnorm_backward_kernel"
+    if w.kind == "prologue":
+        return "gemm_rmsnorm_mxfp8_kernel"
     if threads_per_row == 32:
         return "rowwarp_rmsnorm_fp8_kernel"
     if (not threads_per_row and not w.residual and w.M >= 4096 and w.H <= 8192
@@ -75,6 +77,9 @@ def parse_args():
     ap.add_argument("--workload", default=None,
                     help=f"default {DEFAULT_WORKLOAD} (strong scaling over the ranks)")
     ap.add_argument("--threads-per-row", type=int, default=0)
+    ap.add_argument("--rows", type=int, default=0,
+                    help="rows a rank processes (0: the workload's own split); a smaller "
+                         "case of the same kernel for profiling")
     ap.add_argument("--e2e-steps", type=int, default=0, help="0: min(steps, 20)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -211,6 +216,13 @@ def workload_rows(w, world: int, rank: int):
     return w.M, "weak"
 
 
+def rows_override(args, w, M: int, scaling: str):
+    """--rows R: R rows a rank, weak scaling (a smaller case of the same kernel)."""
+    if args.rows <= 0:
+        return M, scaling
+    return args.rows, "weak"
+
+
 def n_workspaces(w, M) -> int:
     """Workspaces rotated between steps so a step never finds its data in L2."""
     return max(2, math.ceil(3 * L2_BYTES / w.bytes_moved(M)))
@@ -234,12 +246,15 @@ def bench_config(args, w, M: int, world: int, scaling: str) -> dict:
                            else "a full batch per rank") + ", no data-path collective"),
         "l2": f"rotating {n_ws} workspaces of {bytes_step / 1e6:.1f} MB "
               f"({n_ws * bytes_step / 1e6:.0f} MB > L2 {L2_BYTES / 1e6:.0f} MB)",
+        **({"N": w.N} if w.kind == "prologue" else {}),
         "threads_per_row": args.threads_per_row or "auto",
         "launch": "one CUDA graph of the K launches" if args.graph else "eager launches",
     }
 
 
 def dtype_of(w) -> str:
+    if w.kind == "prologue":
+        return "bf16 in, fp32 statistics, e4m3 x e4m3 MXFP8 MMA, fp32 accumulate, bf16 out"
     return ("bf16 gradients, fp32 sums, e4m3 dx" if w.kind == "bwd"
             else "bf16 in, fp32 statistics, e4m3 out")
 
@@ -254,6 +269,22 @@ class Workspace:
             self.x = src["x"].clone()
             self.out = torch.empty_like(self.x)
             self.res = None
+            return
+        if w.kind == "prologue":
+            from thingy_b200.ops import launch_rms_norm_fp8
+
+            # each workspace has its own copy of the GEMM weight, so a step
+            # never finds it in L2 (a decode step reads a new layer's weight)
+            self.x = src["x"].clone()
+            self.d = torch.empty(M, w.N, dtype=torch.bfloat16, device=device)
+            self.qb = torch.empty(w.N, w.H, dtype=torch.float8_e4m3fn, device=device)
+            self.sb = tb.empty_scale(w.N, w.H, 32, "e8m0", "mx", device)
+            launch_rms_norm_fp8(src["gemm_weight"], None, 0.0, q=self.qb, scale=self.sb,
+                                group_size=32, scale_format="e8m0", scale_layout="mx",
+                                normalize=False)
+            # the two-kernel path's intermediate (only the unfused comparison uses it)
+            self.q = torch.empty(M, w.H, dtype=torch.float8_e4m3fn, device=device)
+            self.scale = tb.empty_scale(M, w.H, 32, "e8m0", "mx", device)
             return
         if w.kind == "bwd":
             from thingy_b200.ops import backward_workspace_bytes
@@ -277,10 +308,12 @@ class Workspace:
         self.res_out = torch.empty_like(self.x) if self.res is not None else None
 
 
-def device_run(args, w, M, src, device, local_rank, world, K):
+def device_run(args, w, M, src, device, local_rank, world, K, unfused=False):
     """W warm-up steps, then K timed steps (CUDA events on the launch stream).
 
-    Returns (per-step ms of this rank, clock summary or None)."""
+    unfused (prologue workloads): the two-kernel path instead of the fused
+    kernel, for comparison. Returns (per-step ms of this rank, clock summary or None)."""
+    from thingy_b200.gemm import mxfp8_gemm, rms_norm_mxfp8_gemm
     from thingy_b200.ops import launch_rms_norm, launch_rms_norm_backward, launch_rms_norm_fp8
 
     import torch.distributed as dist
@@ -294,6 +327,14 @@ def device_run(args, w, M, src, device, local_rank, world, K):
         s = ws[i % n_ws]
         if w.kind == "rms_f32":
             launch_rms_norm(s.x, weight, w.eps, s.out, threads_per_row=args.threads_per_row)
+            return
+        if w.kind == "prologue":
+            if unfused:  # RMSNorm + MXFP8 to HBM, then the GEMM reads it back
+                launch_rms_norm_fp8(s.x, weight, w.eps, q=s.q, scale=s.scale, group_size=32,
+                                    scale_format="e8m0", scale_layout="mx")
+                mxfp8_gemm(s.q, s.scale, s.qb, s.sb, out=s.d)
+            else:
+                rms_norm_mxfp8_gemm(s.x, weight, w.eps, s.qb, s.sb, out=s.d)
             return
         if w.kind == "bwd":  # backward: two kernels (rows, then the d_weight reduction)
             launch_rms_norm_backward(
@@ -365,10 +406,12 @@ def device_run(args, w, M, src, device, local_rank, world, K):
     return total_ms / K, (clocks.summary(window) if clocks else None)
 
 
-def roofline(w, bytes_step, launch_ms, threads_per_row) -> dict:
+def roofline(w, bytes_step, launch_ms, threads_per_row, M=None) -> dict:
     peak, peak_src = measured_peak()
     achieved = bytes_step / (launch_ms * 1e-3) / 1e9
     traffic, traffic_src = ncu_traffic(w.name)
+    if traffic is not None and M is not None and M != w.M:
+        traffic = round(traffic * M / w.M)  # DRAM bytes grow with the rows a launch processes
     return {
         "bound": "hbm",
         "achieved": round(achieved, 2),
@@ -397,13 +440,23 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(device)
     _lib.load()
     w = WORKLOADS[args.workload]
-    M, scaling = workload_rows(w, world, rank)
+    M, scaling = rows_override(args, w, *workload_rows(w, world, rank))
     src = make_inputs(w, M, device=device, seed=0, row_offset=rank)
     weight = src["weight"]
     bytes_step = w.bytes_moved(M)
     K = args.steps
     step_ms, clocks = device_run(args, w, M, src, device, local_rank, world, K)
     t_step_ms = max_over_ranks(step_ms, device) if world > 1 else step_ms
+    unfused = None
+    if w.kind == "prologue":  # the same step as two kernels, for comparison
+        u_ms, _ = device_run(args, w, M, src, device, local_rank, world, K, unfused=True)
+        u_ms = max_over_ranks(u_ms, device) if world > 1 else u_ms
+        unfused = {
+            "ms_per_step": round(u_ms, 5),
+            "launches_per_step": 2,
+            "path": "cutie_rms_norm_fp8 (1x32, e8m0, swizzled) to HBM, then cutie_gemm_mxfp8",
+            "fused_speedup": round(u_ms / t_step_ms, 3),
+        }
 
     # all ranks' algorithmic bytes (strong scaling: the whole batch, plus one
     # weight read per extra rank) over the slowest rank's step time
@@ -511,7 +564,7 @@ def run_ours(args, rank, world, local_rank):
         "tokens_per_s": round(rows_total / (t_step_ms * 1e-3), 1),
         "pct_of_hbm_peak": round(100 * value / (peak * world), 2),
         "pct_of_8tbs": round(100 * value / (8000.0 * world), 2),
-        "roofline": roofline(w, bytes_step, t_step_ms, args.threads_per_row),
+        "roofline": roofline(w, bytes_step, t_step_ms, args.threads_per_row, M),
         "cpu_baseline": cpu,
         "e2e": e2e,
         "gpu_launches": K * (2 if w.kind == "bwd" else 1),
@@ -519,6 +572,8 @@ def run_ours(args, rank, world, local_rank):
     }
     if secondary is not None:
         result["secondary"] = secondary
+    if unfused is not None:
+        result["unfused"] = unfused
     if rank == 0:
         print(json.dumps(result), flush=True)
 
@@ -595,7 +650,7 @@ def run_reference(args, rank, world):
     from thingy_b200.workloads import WORKLOADS
 
     w = WORKLOADS[args.workload]
-    M, scaling = workload_rows(w, world, rank)
+    M, scaling = rows_override(args, w, *workload_rows(w, world, rank))
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     # bounded sample per step so W + K steps finish in a few minutes

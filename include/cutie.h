@@ -244,6 +244,31 @@ CUTIE_API int cutie_gemm_mxfp8(const void* a, int64_t lda, const void* a_scale,
                                void* stream);
 
 /*
+ * RMSNorm -> MXFP8 quantization -> block-scaled GEMM in ONE kernel: the
+ * norm-and-quantize step becomes the GEMM's A-operand prologue, so the FP8
+ * codes and scales of the activation never leave the chip (no counterpart in
+ * the reference; it composes rms_norm_reference, src/cutie/rms_norm/bench.py:
+ * 58-65, the 1x32 UE8M0 quantizer rule of src/cutie/vendor/prime_rl/
+ * fp8_utils.py:50-57 with gran_k 32, and the GEMM its output feeds):
+ *   A = cutie_rms_norm_fp8(x, weight, eps, group 32, e8m0, swizzled) codes,
+ *   D[m, n] = bf16( sum_k A[m, k] 2^(sA[m, k/32] - 127) * b[n, k] 2^(sB[n, k/32] - 127) )
+ * x: bf16 [M, K] (ldx elements, 16-byte aligned rows), weight: bf16 [K];
+ * b / b_scale / d as cutie_gemm_mxfp8. q / q_scale: both NULL, or an e4m3
+ * [M, K] buffer (ldq bytes) and a swizzled e8m0 scale buffer that receive A
+ * and its scales as cutie_rms_norm_fp8 would write them (for a backward pass
+ * that keeps the quantized activation). N and K multiples of 128,
+ * K <= 65536. The CTAs that share 128 rows of x run as a thread-block cluster
+ * (8, 4, 2 or 1 CTAs along N, the largest that divides N / 128) and quantize
+ * each A tile once between them. Asynchronous on `stream`; nothing is
+ * allocated.
+ */
+CUTIE_API int cutie_rms_norm_mxfp8_gemm(const void* x, int64_t ldx, const void* weight,
+                                        float eps, const void* b, int64_t ldb,
+                                        const void* b_scale, void* d, int64_t ldd, int64_t M,
+                                        int64_t N, int64_t K, void* q, int64_t ldq,
+                                        void* q_scale, void* stream);
+
+/*
  * Device-side status of this library's kernels on the current device: 0 when
  * no kernel has hit a failure since the last clear; otherwise the first error
  * code recorded (1 = a bulk-copy wait ran out: a row never arrived in shared

@@ -36,6 +36,7 @@ EXPORTED_SYMBOLS = (
     "cutie_rms_norm_backward_workspace",
     "cutie_rms_norm_backward_noalloc",
     "cutie_gemm_mxfp8",
+    "cutie_rms_norm_mxfp8_gemm",
     "cutie_device_error",
     "cutie_set_wait_limit",
     "cutie_last_error",
@@ -74,6 +75,11 @@ _SIGNATURES = {
     ),
     "cutie_gemm_mxfp8": (
         _int, [_ptr, _i64, _ptr, _ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, _i64, _ptr],
+    ),
+    "cutie_rms_norm_mxfp8_gemm": (
+        _int,
+        [_ptr, _i64, _ptr, _f32, _ptr, _i64, _ptr, _ptr, _i64, _i64, _i64, _i64, _ptr, _i64,
+         _ptr, _ptr],
     ),
     "cutie_device_error": (_int, [_int]),
     "cutie_set_wait_limit": (_i64, [_i64]),

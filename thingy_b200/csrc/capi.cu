@@ -754,12 +754,55 @@ extern "C" int cutie_gemm_mxfp8(const void* a, int64_t lda, const void* a_scale,
   return CUTIE_OK;
 }
 
+extern "C" int cutie_rms_norm_mxfp8_gemm(const void* x, int64_t ldx, const void* weight,
+                                         float eps, const void* b, int64_t ldb,
+                                         const void* b_scale, void* d, int64_t ldd, int64_t M,
+                                         int64_t N, int64_t K, void* q, int64_t ldq,
+                                         void* q_scale, void* stream) {
+  g_err[0] = '\0';
+  if (M < 0 || N <= 0 || K <= 0)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "need M >= 0, N > 0 and K > 0 (got %lld, %lld, %lld)",
+                (long long)M, (long long)N, (long long)K);
+  if (N % 128 != 0 || K % 128 != 0)
+    return fail(CUTIE_ERR_UNSUPPORTED, "N and K must be multiples of 128 (got N=%lld, K=%lld)",
+                (long long)N, (long long)K);
+  if (K > 65536)
+    return fail(CUTIE_ERR_UNSUPPORTED, "K must be at most 65536 (got %lld)", (long long)K);
+  if (M > INT32_MAX || N > INT32_MAX)
+    return fail(CUTIE_ERR_UNSUPPORTED, "M and N must be below 2^31");
+  if (!std::isfinite(eps) || eps < 0.0f)
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "eps must be finite and >= 0");
+  if ((q == nullptr) != (q_scale == nullptr))
+    return fail(CUTIE_ERR_INVALID_ARGUMENT, "q and q_scale must be given together");
+  if (M == 0) return CUTIE_OK;
+  int rc;
+  if ((rc = check_matrix("x", x, ldx, K, 16, 8)) != CUTIE_OK) return rc;
+  if (weight == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "weight is NULL");
+  if (!aligned(weight, 16)) return fail(CUTIE_ERR_ALIGNMENT, "weight must be 16-byte aligned");
+  if ((rc = check_matrix("b", b, ldb, K, 16, 16)) != CUTIE_OK) return rc;
+  if ((rc = check_matrix("d", d, ldd, N, 16, 8)) != CUTIE_OK) return rc;
+  if (b_scale == nullptr) return fail(CUTIE_ERR_INVALID_ARGUMENT, "b_scale is NULL");
+  if (!aligned(b_scale, 16))
+    return fail(CUTIE_ERR_ALIGNMENT, "the swizzled scale buffers must be 16-byte aligned");
+  if (q != nullptr) {
+    if ((rc = check_matrix("q", q, ldq, K, 16, 16)) != CUTIE_OK) return rc;
+    if (!aligned(q_scale, 16))
+      return fail(CUTIE_ERR_ALIGNMENT, "the swizzled scale buffers must be 16-byte aligned");
+  }
+  const char* why = "";
+  rc = gemm_rmsnorm_mxfp8(x, ldx, weight, eps, b, ldb, b_scale, d, ldd, M, N, K, q, ldq, q_scale,
+                          g_wait_limit, static_cast<cudaStream_t>(stream), &why);
+  if (rc != CUTIE_OK) return fail(rc, "rms_norm mxfp8 gemm: %s", why);
+  return CUTIE_OK;
+}
+
 extern "C" int cutie_device_error(int clear) {
   g_err[0] = '\0';
   int any = 0;
   cudaError_t (*readers[])(int*, bool) = {device_error_none, device_error_token, device_error_g32,
                                           device_error_g64, device_error_g128,
-                                          device_error_bwd,  device_error_gemm};
+                                          device_error_bwd,  device_error_gemm,
+                                          device_error_prologue};
   for (auto read : readers) {
     int v = 0;
     const cudaError_t e = read(&v, clear != 0);

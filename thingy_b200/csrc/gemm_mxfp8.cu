@@ -32,13 +32,9 @@
 // CTA's abort flag and the device error word; the producer stops issuing and
 // lets its copies in flight land, the MMA thread commits what it issued and
 // the epilogue waits for that before tensor memory is freed.
-#include <cuda.h>
-#include <cudaTypedefs.h>
-
-#include <mutex>
-
 #include "cutie.h"
 #include "launch.cuh"
+#include "tcgen05.cuh"
 
 namespace cutie {
 
@@ -56,61 +52,18 @@ constexpr uint32_t kAccCol = 0, kSfCol = 128;  // scales of stage s: kSfCol + 8 
 constexpr int kThreads = 128;
 constexpr size_t kSmemBytes = kStages * kStageBytes + 1024;  // + alignment to 1 KB
 
-__device__ __forceinline__ void fence_tc_before() {
-  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
-}
-__device__ __forceinline__ void fence_tc_after() {
-  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
-}
-
-// Shared-memory operand descriptor (tcgen05 matrix descriptor): start
-// address, leading and stride byte offsets (16-byte units), version 1, layout.
-__device__ __forceinline__ uint64_t smem_desc(uint32_t addr, uint32_t lbo, uint32_t sbo,
-                                              uint32_t layout) {
-  return (uint64_t)((addr >> 4) & 0x3FFFu) | ((uint64_t)((lbo >> 4) & 0x3FFFu) << 16) |
-         ((uint64_t)((sbo >> 4) & 0x3FFFu) << 32) | (1ull << 46) | ((uint64_t)layout << 61);
-}
-constexpr uint32_t kLayoutSw128 = 2, kLayoutNone = 0;
-
-// Instruction descriptor of kind::mxf8f6f4.block_scale: e4m3 x e4m3, both
-// K-major, M = 128, N = 128, e8m0 scales, scale ids for A and B.
+using tc::kLayoutNone;
+using tc::kLayoutSw128;
+using tc::mma_mxf8;
+using tc::smem_desc;
+using tc::tma_load_2d;
+__device__ __forceinline__ void fence_tc_before() { tc::fence_before(); }
+__device__ __forceinline__ void fence_tc_after() { tc::fence_after(); }
 __device__ __forceinline__ uint32_t instr_desc(uint32_t sf_id) {
-  return (sf_id << 4)              // B scale id
-         | (0u << 7) | (0u << 10)  // A, B: e4m3
-         | ((uint32_t)(kBN >> 3) << 17) | (1u << 23)  // N, scales e8m0
-         | ((uint32_t)(kBM >> 4) << 24) | (sf_id << 29);  // M, A scale id
+  return tc::mxf8_idesc(kBM, kBN, sf_id);
 }
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, int c0, int c1,
-                                            uint32_t bar) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(bar)
-      : "memory");
-}
-
-__device__ __forceinline__ void mma_mxf8(uint32_t d_tmem, uint64_t adesc, uint64_t bdesc,
-                                         uint32_t idesc, uint32_t sfa_tmem, uint32_t sfb_tmem,
-                                         uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
-      " tcgen05.mma.cta_group::1.kind::mxf8f6f4.block_scale [%0], %1, %2, %3, [%5], [%6], p;\n}" ::
-          "r"(d_tmem),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate), "r"(sfa_tmem), "r"(sfb_tmem)
-      : "memory");
-}
-
-__device__ __forceinline__ void tc_copy_sf(uint32_t tmem_col, uint64_t src_desc) {
-  asm volatile("tcgen05.cp.cta_group::1.32x128b.warpx4 [%0], %1;" ::"r"(tmem_col), "l"(src_desc)
-               : "memory");
-}
-
-__device__ __forceinline__ void tc_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
-}
+__device__ __forceinline__ void tc_copy_sf(uint32_t col, uint64_t desc) { tc::copy_sf(col, desc); }
+__device__ __forceinline__ void tc_commit(uint32_t bar) { tc::commit(bar); }
 
 // Waits that give up after `limit` cycles or at once when the abort flag is
 // set; giving up sets the flag.
@@ -264,34 +217,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                  : "memory");
 }
 
-// cuTensorMapEncodeTiled from the driver, found through the runtime (no
-// link-time dependency on libcuda).
-PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
-  static std::once_flag once;
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  std::call_once(once, [] {
-    void* p = nullptr;
-    cudaDriverEntryPointQueryResult q{};
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
-            cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  });
-  return fn;
-}
-
-// A [rows, K] e4m3 operand, K contiguous, `ld` bytes between rows: 128 x 128
-// boxes, 128-byte swizzle, zero fill past the last row.
 bool encode_operand(CUtensorMap* map, const void* ptr, int64_t rows, int64_t K, int64_t ld) {
-  auto fn = encode_fn();
-  if (fn == nullptr) return false;
-  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
-  const cuuint64_t strides[1] = {(cuuint64_t)ld};
-  const cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)kBM};
-  const cuuint32_t estr[2] = {1, 1};
-  return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box,
-            estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return tc::encode_e4m3_operand(map, ptr, rows, K, ld);
 }
 
 }  // namespace

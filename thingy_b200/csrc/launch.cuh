@@ -298,6 +298,15 @@ int gemm_mxfp8(const void* a, int64_t lda, const void* a_scale, const void* b, i
                cudaStream_t stream, const char** why);
 cudaError_t device_error_gemm(int* out, bool clear);
 
+// Fused RMSNorm -> MXFP8 -> block-scaled GEMM (gemm_prologue.cu): arguments
+// checked by the caller (q and q_scale both null or both set); same status
+// convention as gemm_mxfp8.
+int gemm_rmsnorm_mxfp8(const void* x, int64_t ldx, const void* weight, float eps, const void* b,
+                       int64_t ldb, const void* b_scale, void* d, int64_t ldd, int64_t M,
+                       int64_t N, int64_t K, void* q, int64_t ldq, void* q_scale,
+                       long long wait_limit, cudaStream_t stream, const char** why);
+cudaError_t device_error_prologue(int* out, bool clear);
+
 // max_grid > 0 caps the CTAs (and so the rows of partial sums in a.partial).
 cudaError_t launch_backward(const BwdArgs& a, float eps, bool dw_wanted, uint16_t* dw,
                             int max_grid, cudaStream_t st);

@@ -1,4 +1,5 @@
-"""The downstream consumer of the path's MXFP8 output: a block-scaled FP8 GEMM.
+"""The downstream consumer of the path's MXFP8 output: a block-scaled FP8 GEMM,
+and the same GEMM with RMSNorm + MXFP8 quantization fused in as its prologue.
 
 ``mxfp8_gemm(a, a_scale, b, b_scale)`` multiplies e4m3 codes with 1x32 e8m0
 scales in the Blackwell swizzled layout (what ``rms_norm_fp8(...,
@@ -58,5 +59,68 @@ def mxfp8_gemm(a: torch.Tensor, a_scale: torch.Tensor, b: torch.Tensor, b_scale:
         status = lib.cutie_gemm_mxfp8(
             a.data_ptr(), lda, a_scale.data_ptr(), b.data_ptr(), ldb, b_scale.data_ptr(),
             out.data_ptr(), ldd, M, N, K, torch.cuda.current_stream(a.device).cuda_stream)
+    _lib.check(status)
+    return out
+
+
+def rms_norm_mxfp8_gemm(x: torch.Tensor, weight: torch.Tensor, eps: float, b: torch.Tensor,
+                        b_scale: torch.Tensor, out: torch.Tensor | None = None,
+                        q: torch.Tensor | None = None,
+                        q_scale: torch.Tensor | None = None) -> torch.Tensor:
+    """bf16 [M, N] = mxfp8_gemm(*rms_norm_fp8(x, weight, eps, group 32, e8m0, mx), b, b_scale).
+
+    One kernel (``cutie_rms_norm_mxfp8_gemm``): the RMSNorm and the 1x32 UE8M0
+    quantization of x run inside the GEMM as the producer of its A tiles, so
+    the FP8 activation is never written to HBM. x: bf16 [M, K] (rows
+    contiguous); weight: bf16 [K]; b / b_scale: the e4m3 weight [N, K] and
+    its swizzled e8m0 scales, as for ``mxfp8_gemm``. ``q`` (e4m3 [M, K]) and
+    ``q_scale`` (swizzled e8m0, ``empty_scale(M, K, 32, "e8m0", "mx")``),
+    if given, also receive the quantized activation, bit for bit what
+    ``rms_norm_fp8`` returns for the same x. Runs on the current stream.
+    """
+    if not isinstance(x, torch.Tensor) or x.dim() != 2 or not x.is_cuda or x.dtype != torch.bfloat16:
+        raise ValueError("x must be a 2-D bf16 CUDA tensor")
+    M, K = x.shape
+    if M > 0 and K > 1 and x.stride(1) != 1:
+        raise ValueError("x must be contiguous along K")
+    ldx = max(x.stride(0), K) if M > 1 else K
+    if weight.shape != (K,) or weight.dtype != torch.bfloat16 or weight.device != x.device \
+            or not weight.is_contiguous():
+        raise ValueError(f"weight must be a contiguous bf16 [{K}] tensor on {x.device}")
+    N = b.shape[0]
+    ldb = _operand("b", b, K)
+    if b_scale.dtype not in E8M0_DTYPES or not b_scale.is_contiguous() or b_scale.device != x.device:
+        raise ValueError(f"b_scale must be contiguous e8m0 (or uint8) bytes on {x.device}")
+    if b_scale.numel() < mx_swizzled_size(N, -(-K // 32)):
+        raise ValueError(f"b_scale holds {b_scale.numel()} bytes, the swizzled layout needs "
+                         f"{mx_swizzled_size(N, -(-K // 32))}")
+    if b.device != x.device:
+        raise ValueError("x and b must be on the same device")
+    if out is None:
+        out = torch.empty(M, N, dtype=torch.bfloat16, device=x.device)
+    elif out.shape != (M, N) or out.dtype != torch.bfloat16 or (N > 1 and out.stride(1) != 1):
+        raise ValueError(f"out must be a bf16 [{M}, {N}] tensor contiguous along N")
+    ldd = max(out.stride(0), N) if M > 1 else N
+    if (q is None) != (q_scale is None):
+        raise ValueError("q and q_scale must be given together")
+    ldq = 0
+    if q is not None:
+        ldq = _operand("q", q, K)
+        if q.shape[0] != M:
+            raise ValueError(f"q must be [{M}, {K}]")
+        if q_scale.dtype not in E8M0_DTYPES or not q_scale.is_contiguous() \
+                or q_scale.device != x.device:
+            raise ValueError(f"q_scale must be contiguous e8m0 (or uint8) bytes on {x.device}")
+        if q_scale.numel() < mx_swizzled_size(M, -(-K // 32)):
+            raise ValueError(f"q_scale holds {q_scale.numel()} bytes, the swizzled layout needs "
+                             f"{mx_swizzled_size(M, -(-K // 32))}")
+    lib = _lib.load()
+    with torch.cuda.device(x.device):
+        status = lib.cutie_rms_norm_mxfp8_gemm(
+            x.data_ptr(), ldx, weight.data_ptr(), float(eps), b.data_ptr(), ldb,
+            b_scale.data_ptr(), out.data_ptr(), ldd, M, N, K,
+            None if q is None else q.data_ptr(), ldq,
+            None if q_scale is None else q_scale.data_ptr(),
+            torch.cuda.current_stream(x.device).cuda_stream)
     _lib.check(status)
     return out

@@ -23,6 +23,12 @@ bit for bit (parity tests build inputs on the CPU and copy them to the GPU).
                          1x128 FP8 over row shards, x ~ N(0,1) with
                          round(0.001*H) outlier channels x50, column-major
                          fp32 scales, eps 1e-6
+  prologue_mx32_5120x5120
+                         config 4's decode MXFP8 rows (M in {1, 8, 32, 128},
+                         H = K = 5120, Student-t) fed to a 5120 x 5120
+                         block-scaled FP8 GEMM: RMSNorm -> MXFP8 -> GEMM in
+                         one kernel; the GEMM weight is bf16 0.05*N(0,1)
+                         quantized to MXFP8 by this path
 Weights are bf16 1 + 0.1*N(0,1) everywhere.
 """
 
@@ -44,8 +50,10 @@ class Workload:
     scale_layout: str
     residual: bool
     dist: str  # "normal", "outliers", "student_t"
-    kind: str = "fused"  # "fused" (bf16 -> fp8), "rms_f32" (standalone fp32 RMSNorm)
-    #                      or "bwd" (backward: gradients of the fused path)
+    kind: str = "fused"  # "fused" (bf16 -> fp8), "rms_f32" (standalone fp32 RMSNorm),
+    #                      "bwd" (backward: gradients of the fused path) or "prologue"
+    #                      (RMSNorm -> MXFP8 -> GEMM with an N x H weight, one kernel)
+    N: int = 0           # GEMM output columns ("prologue" only)
 
     def bytes_moved(self, M: int | None = None) -> int:
         """Algorithmic HBM bytes of one pass: inputs read once, outputs written once.
@@ -58,6 +66,10 @@ class Workload:
         """
         M = self.M if M is None else M
         H = self.H
+        if self.kind == "prologue":
+            # read x, the norm weight, the e4m3 GEMM weight and its e8m0
+            # scales; write D (bf16). The FP8 activation stays on chip.
+            return 2 * M * H + 2 * H + self.N * H + self.N * (H // 32) + 2 * M * self.N
         if self.kind == "rms_f32":  # utils.py:10-19: x and out fp32, weight once
             return 2 * M * H * 4 + H * 4
         if self.kind == "bwd":
@@ -90,6 +102,8 @@ WORKLOADS = {
                  "outliers"),
         Workload("bwd_residual_g128_16384x7168", 16384, 7168, 1e-6, 128, "fp32", "col", True,
                  "normal", kind="bwd"),
+        Workload("prologue_mx32_5120x5120", 128, 5120, 1e-6, 32, "e8m0", "mx", False,
+                 "student_t", kind="prologue", N=5120),
         *(
             Workload(f"rmsnorm_f32_{m}x{h}", m, h, 1e-5, None, "fp32", "row", False, "normal",
                      kind="rms_f32")
@@ -144,6 +158,13 @@ def make_inputs(w: Workload, M: int | None = None, *, device="cpu", seed: int = 
             gen.manual_seed(seed * 1_000_003 + row_offset)
         x = torch.randn((M, H), generator=gen, device=device)
         return {"x": x, "weight": torch.randn(H, generator=gen, device=device), "eps": w.eps}
+    if w.kind == "prologue":  # the decode rows plus the GEMM weight
+        weight = _weight(H, gen, device)
+        gemm_w = (0.05 * torch.randn((w.N, H), generator=gen, device=device)).to(torch.bfloat16)
+        if row_offset:
+            gen.manual_seed(seed * 1_000_003 + row_offset)
+        x = _student_t((M, H), 4, gen, device)
+        return {"x": x.to(torch.bfloat16), "weight": weight, "eps": w.eps, "gemm_weight": gemm_w}
     weight = _weight(H, gen, device)
     outliers = None
     if w.dist == "outliers":
