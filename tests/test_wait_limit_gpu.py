@@ -87,3 +87,31 @@ def test_backward_wait_runs_out_then_clean_launch():
             continue
         assert torch.equal(a.view(torch.uint8) if a.dtype == torch.float8_e4m3fn else a,
                            b.view(torch.uint8) if b.dtype == torch.float8_e4m3fn else b)
+
+
+@pytest.mark.parametrize("M,N,K", [(8, 5120, 5120), (200, 512, 2048)])
+def test_fused_gemm_wait_runs_out_then_clean_launch(M, N, K):
+    """The fused RMSNorm -> MXFP8 -> GEMM kernel (thread-block clusters over K):
+    with every wait giving up at once, each CTA still meets its cluster barriers,
+    lets its own copies land and records code 1; the next launch is unaffected."""
+    from thingy_b200.gemm import rms_norm_mxfp8_gemm
+    from thingy_b200.ops import launch_rms_norm_fp8
+
+    assert _lib.device_error(clear=True) == 0
+    inp = exact_sum_inputs(M, K, residual=False, seed=M + K)
+    x, w = inp["x"].cuda(), inp["weight"].cuda()
+    g = torch.Generator().manual_seed(9)
+    W = (0.05 * torch.randn(N, K, generator=g)).to(torch.bfloat16).cuda()
+    qb = torch.empty(N, K, dtype=torch.float8_e4m3fn, device="cuda")
+    sb = tb.empty_scale(N, K, 32, "e8m0", "mx", "cuda")
+    launch_rms_norm_fp8(W, None, 0.0, q=qb, scale=sb, group_size=32, scale_format="e8m0",
+                        scale_layout="mx", normalize=False)
+    ref = rms_norm_mxfp8_gemm(x, w, 1e-6, qb, sb, fused=True)
+    torch.cuda.synchronize()
+    assert _lib.device_error(clear=True) == 0
+    _run_with_limit(lambda: rms_norm_mxfp8_gemm(x, w, 1e-6, qb, sb, fused=True), -1)
+    assert _lib.device_error(clear=True) == 1, "no wait of the fused GEMM ran out"
+    got = rms_norm_mxfp8_gemm(x, w, 1e-6, qb, sb, fused=True)
+    torch.cuda.synchronize()
+    assert _lib.device_error(clear=True) == 0
+    assert torch.equal(ref, got)
