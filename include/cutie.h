@@ -203,7 +203,11 @@ CUTIE_API size_t cutie_rms_norm_backward_workspace(int64_t M, int64_t H);
  * process exits. Its CTAs are capped so that their rows of H partial sums
  * fit (2^20 / H CTAs, e.g. 146 at H = 7168), so d_weight is summed in a
  * different grouping than cutie_rms_norm_backward's (the same bound on the
- * error; dx, q and scale are identical). Sizes: as cutie_rms_norm_backward
+ * error; dx, q and scale are identical). The cap costs time where it is
+ * below the regular grid: measured on a B200 (residual gradient, 1x128 FP8
+ * copy of dx) 210.6 against 183.4 us at 16384 x 7168 (146 CTAs), 122.8
+ * against 116.6 us at 16384 x 4096, 881 against 236 us at 2048 x 32768
+ * (32 CTAs). Sizes: as cutie_rms_norm_backward
  * (H <= 32768, which always fits the array); a larger H is refused with
  * CUTIE_ERR_UNSUPPORTED. Every row of the array that a call reads was
  * written by that call, so nothing needs clearing between calls.
