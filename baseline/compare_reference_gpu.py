@@ -1,8 +1,10 @@
 """The reference's own GPU kernels beside this repo's, same box, same shapes, same buffers.
 
 Runs on a B200 with the reference installed into ``baseline/_ref`` (the
-git-ignored install of S1ro1/thingy that travels with the tree; see
-DESIGN.md for how it was installed). Three implementations of the
+git-ignored install of S1ro1/thingy that travels with the tree: pip's
+``--target`` install of the reference's sources; its own build backend,
+uv_build, is not needed by anything here, so any PEP 517 backend that copies
+``src/cutie`` and ``src/kittie`` unchanged will do). Three implementations of the
 reference's fused contract (src/cutie/rms_norm/bench.py:10-15: residual add,
 RMSNorm, 1x128 FP8 with fp32 row-major scales, writing q, scale,
 residual_out and normalized) are timed on the same rotating workspaces:
