@@ -201,3 +201,63 @@ def test_wait_limit_is_per_thread_and_restorable(lib):
     assert seen == [default]  # the other thread never saw 123
     assert lib.cutie_set_wait_limit(0) == 123
     assert _lib.set_wait_limit(0) == default
+
+
+def gemm(lib, **kw):
+    args = dict(a=FAKE, lda=1024, a_scale=FAKE, b=FAKE, ldb=1024, b_scale=FAKE, d=FAKE,
+                ldd=256, M=4, N=256, K=1024, stream=None)
+    args.update(kw)
+    return lib.cutie_gemm_mxfp8(*args.values())
+
+
+def fused_gemm(lib, **kw):
+    args = dict(x=FAKE, ldx=1024, weight=FAKE, eps=1e-6, b=FAKE, ldb=1024, b_scale=FAKE, d=FAKE,
+                ldd=256, M=4, N=256, K=1024, q=None, ldq=0, q_scale=None, stream=None)
+    args.update(kw)
+    return lib.cutie_rms_norm_mxfp8_gemm(*args.values())
+
+
+@pytest.mark.parametrize(
+    "kw,code,needle",
+    [
+        ({"N": 192, "ldd": 192}, _lib.ERR_UNSUPPORTED, "multiples of 128"),
+        ({"K": 1000, "lda": 1000, "ldb": 1000}, _lib.ERR_UNSUPPORTED, "multiples of 128"),
+        ({"M": -1}, _lib.ERR_INVALID_ARGUMENT, "M >= 0"),
+        ({"a": MISALIGNED}, _lib.ERR_ALIGNMENT, "16-byte aligned"),
+        ({"lda": 1000}, _lib.ERR_INVALID_ARGUMENT, "leading dimension"),
+        ({"b_scale": None}, _lib.ERR_INVALID_ARGUMENT, "NULL"),
+        ({"a_scale": MISALIGNED}, _lib.ERR_ALIGNMENT, "scale"),
+    ],
+)
+def test_gemm_argument_errors(lib, kw, code, needle):
+    """The MXFP8 GEMM validates its arguments before any CUDA call."""
+    assert gemm(lib, **kw) == code
+    assert needle in lib.cutie_last_error().decode()
+
+
+@pytest.mark.parametrize(
+    "kw,code,needle",
+    [
+        ({"N": 192, "ldd": 192}, _lib.ERR_UNSUPPORTED, "multiples of 128"),
+        ({"K": 1000, "ldx": 1000, "ldb": 1000}, _lib.ERR_UNSUPPORTED, "multiples of 128"),
+        ({"K": 131072, "ldx": 131072, "ldb": 131072}, _lib.ERR_UNSUPPORTED, "65536"),
+        ({"M": -1}, _lib.ERR_INVALID_ARGUMENT, "M >= 0"),
+        ({"eps": float("nan")}, _lib.ERR_INVALID_ARGUMENT, "eps"),
+        ({"q": FAKE, "ldq": 1024}, _lib.ERR_INVALID_ARGUMENT, "together"),
+        ({"x": MISALIGNED}, _lib.ERR_ALIGNMENT, "16-byte aligned"),
+        ({"weight": MISALIGNED}, _lib.ERR_ALIGNMENT, "weight"),
+        ({"weight": None}, _lib.ERR_INVALID_ARGUMENT, "weight is NULL"),
+        ({"ldx": 1020}, _lib.ERR_INVALID_ARGUMENT, "leading dimension"),
+        ({"q": FAKE, "ldq": 1024, "q_scale": MISALIGNED}, _lib.ERR_ALIGNMENT, "scale"),
+    ],
+)
+def test_fused_gemm_argument_errors(lib, kw, code, needle):
+    """The fused RMSNorm -> MXFP8 -> GEMM validates its arguments before any CUDA call."""
+    assert fused_gemm(lib, **kw) == code
+    assert needle in lib.cutie_last_error().decode()
+
+
+def test_gemms_with_no_rows_are_no_ops(lib):
+    assert gemm(lib, M=0, a=None, a_scale=None, b=None, b_scale=None, d=None) == _lib.OK
+    assert fused_gemm(lib, M=0, x=None, weight=None, b=None, b_scale=None, d=None) == _lib.OK
+    assert lib.cutie_last_error() == b""
