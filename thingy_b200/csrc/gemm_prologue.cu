@@ -66,7 +66,7 @@ constexpr int kTM = 128, kTN = 128, kTK = 128;  // tile; K in elements
 constexpr uint32_t kTile = 16384;               // one 128 x 128 e4m3 tile
 constexpr uint32_t kAtom = 512;                 // one 128 x 4 e8m0 scale atom
 constexpr int kProducerWarps = 4;
-constexpr int kSA = kProducerWarps;  // A stages: one per quantizing warp
+constexpr int kMaxSA = kProducerWarps;  // A stages: one per quantizing warp of pass 2
 constexpr int kProducers = kProducerWarps * 32;
 constexpr int kWarpB = 4, kWarpMma = 5, kWarpX = 6;
 constexpr int kThreads = 7 * 32;
@@ -100,8 +100,11 @@ constexpr int kMaxXS = 16;
 template <int QB>
 struct Plan {
   static constexpr uint32_t kXRegion = QB == 1 ? 32768u : QB == 3 ? 49152u : 65536u;
+  // one A stage per quantizing warp (two warps and a 9-stage weight ring
+  // measured slower from 16 rows on, and no faster below)
+  static constexpr int kSA = kMaxSA;
   static constexpr int SB = QB == 1 ? 7 : QB == 3 ? 6 : 5;  // B ring stages
-  static constexpr uint32_t kOffA = 0;  // after the K loop: the fp32 partial tile (64 KB)
+  static constexpr uint32_t kOffA = 0;  // after the K loop: the fp32 partial rows
   static constexpr uint32_t kOffSfA = kSA * kTile;
   static constexpr uint32_t kOffW = kOffSfA + kSA * kAtom;  // kMaxXS chunks of 128 weights
   static constexpr uint32_t kOffX = kOffW + kMaxXS * 256u;
@@ -111,7 +114,8 @@ struct Plan {
   static constexpr size_t kSmem = kBytes + 1024;  // + alignment of the base to 1 KB
   // the other CTAs' partial tiles (rows with data) fit below kOffSfB
   static constexpr uint32_t kPushArea = kOffSfB;
-  static_assert(kSA * kTile >= kTM * kTN * 4, "the partial tile fits the A stages");
+  // the partial rows (32 QB of them, 512 bytes each) fit the A stages
+  static_assert(kSA * kTile >= 32u * QB * kTN * 4, "the partial tile fits the A stages");
   static_assert(kOffX % 1024 == 0 && kOffB % 1024 == 0, "swizzled tiles on 1 KB boundaries");
   static_assert(kSmem + 6 * 1024 <= 227 * 1024, "shared memory (with the static arrays)");
 };
@@ -128,10 +132,11 @@ __device__ __forceinline__ uint4 ld_cluster_v4(uint32_t addr) {
   return v;
 }
 
-// Byte offset of (row, 4 columns c4) in the fp32 partial tile: column groups
-// outermost, so a warp's 32 rows fill 512 contiguous bytes (no bank conflicts).
-__device__ __forceinline__ uint32_t part_off(int row, int c4) {
-  return ((uint32_t)c4 * kTM + (uint32_t)row) * 16u;
+// Byte offset of (row, 4 columns c4) in the fp32 partial rows (rows < rows_
+// with data): column groups outermost, so a warp's consecutive rows fill
+// contiguous 16-byte slots (no bank conflicts).
+__device__ __forceinline__ uint32_t part_off(int row, int c4, int rows) {
+  return ((uint32_t)c4 * (uint32_t)rows + (uint32_t)row) * 16u;
 }
 
 template <int QB>
@@ -140,7 +145,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                               const __grid_constant__ CUtensorMap map_b, const ProArgs a) {
   using P = Plan<QB>;
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t full_a[kSA], empty_a[kSA];
+  constexpr int kSA = P::kSA;
+  __shared__ __align__(8) uint64_t full_a[kMaxSA], empty_a[kMaxSA];
   __shared__ __align__(8) uint64_t full_b[P::SB], empty_b[P::SB];
   // x_full: in a resident ring one barrier per stage, each completing once;
   // otherwise indexed by x iteration mod 4 (in pass 2 that is a fixed
@@ -378,9 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       asm volatile("bar.sync %0, %1;" ::"n"(kBarProducers), "n"(kProducers) : "memory");
 
-      // ---- pass 2: warp w makes the A tiles of this CTA's K blocks w, w + 4, ...
+      // ---- pass 2: warp w < kSA makes the A tiles of this CTA's K blocks
+      // w, w + kSA, ... (x_full slot it % 4 then always belongs to one warp)
       const bool store_q = a.q != nullptr && blockIdx.x == 0;  // one tile column writes q
-      for (int i = warp; i < kbs; i += kProducerWarps) {
+      for (int i = warp; warp < kSA && i < kbs; i += kSA) {
         const int it = kbs + i, kb = kb0 + i;
         const int sa = i % kSA, xs = resident ? i : it % XS;
         bool ok = resident || mbar_wait_abortable(smem_addr(&x_full[xf(it)]), xp(it), abortp,
@@ -492,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                            "r"(v4[0]), "r"(v4[1]), "r"(v4[2]), "r"(v4[3])
                            : "memory");
             } else {
-              st_smem(base + P::kOffA + part_off(row, c / 4 + k), v4);
+              st_smem(base + P::kOffA + part_off(row, c / 4 + k, Mr), v4);
             }
           }
         }
@@ -510,7 +517,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int k = 0; k < 8; ++k) {
             const uint4 o =
                 push ? ld_smem(base + push_off(p, row, c / 4 + k))
-                     : ld_cluster_v4(tc::mapa(base + P::kOffA + part_off(row, c / 4 + k),
+                     : ld_cluster_v4(tc::mapa(base + P::kOffA + part_off(row, c / 4 + k, Mr),
                                               (uint32_t)p));
             const uint32_t ov[4] = {o.x, o.y, o.z, o.w};
 #pragma unroll
