@@ -55,6 +55,9 @@ def _kernel_name(w, threads_per_row) -> str:
     """The kernel that carries the timed step (the launch shape rules of csrc/capi.cu)."""
     if w.kind == "rms_f32":
         return "rmsnorm_f32_kernel"
+    if w.kind == "rms_bf16":  # the fused kernels without quantization
+        return ("rowstage_rmsnorm_fp8_kernel" if w.M >= 4096 and w.H <= 8192
+                else "pipe_rmsnorm_fp8_kernel")
     if w.kind == "bwd":  # rows of up to 16384 take the bulk-copy ring variant
         return "rmsnorm_backward_ring_kernel" if w.H <= 16384 else "rmsnorm_backward_kernel"
     if w.kind == "prologue":
@@ -253,6 +256,10 @@ def bench_config(args, w, M: int, world: int, scaling: str) -> dict:
 
 
 def dtype_of(w) -> str:
+    if w.kind == "rms_bf16":
+        return "bf16 in, fp32 statistics, bf16 out"
+    if w.kind == "rms_f32":
+        return "fp32"
     if w.kind == "prologue":
         return "bf16 in, fp32 statistics, e4m3 x e4m3 MXFP8 MMA, fp32 accumulate, bf16 out"
     return ("bf16 gradients, fp32 sums, e4m3 dx" if w.kind == "bwd"
@@ -265,7 +272,7 @@ class Workspace:
     def __init__(self, w, M, src, device):
         import thingy_b200 as tb
 
-        if w.kind == "rms_f32":
+        if w.kind in ("rms_f32", "rms_bf16"):
             self.x = src["x"].clone()
             self.out = torch.empty_like(self.x)
             self.res = None
@@ -325,7 +332,7 @@ def device_run(args, w, M, src, device, local_rank, world, K, unfused=False):
 
     def step(i):  # one launch on the current stream
         s = ws[i % n_ws]
-        if w.kind == "rms_f32":
+        if w.kind in ("rms_f32", "rms_bf16"):
             launch_rms_norm(s.x, weight, w.eps, s.out, threads_per_row=args.threads_per_row)
             return
         if w.kind == "prologue":
@@ -604,11 +611,16 @@ def time_oracle(w, rows: int, reps: int):
     times = []
     for _ in range(reps):
         t0 = time.perf_counter()
-        q, s, _, _ = ora.rms_norm_fp8(inp["x"], inp["weight"], w.eps,
-                                      residual=inp.get("residual"), group_size=w.group_size,
-                                      scale_format=w.scale_format)
-        if w.scale_layout != "row":
-            ora.layout_scales(s, w.scale_layout)
+        if w.kind == "rms_bf16":
+            ora.rms_norm_reference(inp["x"], inp["weight"], w.eps)
+        elif w.kind == "rms_f32":
+            ora.rms_norm_f32(inp["x"], inp["weight"], w.eps)
+        else:
+            q, s, _, _ = ora.rms_norm_fp8(inp["x"], inp["weight"], w.eps,
+                                          residual=inp.get("residual"),
+                                          group_size=w.group_size, scale_format=w.scale_format)
+            if w.scale_layout != "row":
+                ora.layout_scales(s, w.scale_layout)
         times.append(time.perf_counter() - t0)
     return times
 

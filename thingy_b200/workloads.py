@@ -12,6 +12,9 @@ bit for bit (parity tests build inputs on the CPU and copy them to the GPU).
   residual_token_32768x8192
                          residual add + per-token FP8, x ~ N(0,1),
                          residual ~ N(0, 4) (sigma 2), eps 1e-5, residual_out
+  rmsnorm_bf16_16384x7168
+                         the standalone bf16 RMSNorm (rms_norm_reference,
+                         bf16 out), x ~ N(0,1), config 2's shape
   rmsnorm_f32_MxH        the standalone fp32 RMSNorm of the reference's older
                          baseline (x, w ~ N(0,1) fp32, eps 1e-5) at the shapes
                          of its published sweep, M in {1024, 4096, 16384},
@@ -50,7 +53,7 @@ class Workload:
     scale_layout: str
     residual: bool
     dist: str  # "normal", "outliers", "student_t"
-    kind: str = "fused"  # "fused" (bf16 -> fp8), "rms_f32" (standalone fp32 RMSNorm),
+    kind: str = "fused"  # "fused" (bf16 -> fp8), "rms_f32" / "rms_bf16" (standalone RMSNorm),
     #                      "bwd" (backward: gradients of the fused path) or "prologue"
     #                      (RMSNorm -> MXFP8 -> GEMM with an N x H weight, one kernel)
     N: int = 0           # GEMM output columns ("prologue" only)
@@ -72,6 +75,8 @@ class Workload:
             return 2 * M * H + 2 * H + self.N * H + self.N * (H // 32) + 2 * M * self.N
         if self.kind == "rms_f32":  # utils.py:10-19: x and out fp32, weight once
             return 2 * M * H * 4 + H * 4
+        if self.kind == "rms_bf16":  # x and out bf16, weight once
+            return 2 * M * H * 2 + H * 2
         if self.kind == "bwd":
             # read d_normalized, r [, d_residual_out], weight; write dx, d_weight
             # [, FP8 codes + scales of dx]. The per-CTA partial sums of d_weight
@@ -110,6 +115,8 @@ WORKLOADS = {
             for m in (1024, 4096, 16384)
             for h in (1024, 3072, 7168)
         ),
+        Workload("rmsnorm_bf16_16384x7168", 16384, 7168, 1e-6, None, "fp32", "row", False,
+                 "normal", kind="rms_bf16"),
     )
 }
 
@@ -153,6 +160,12 @@ def make_inputs(w: Workload, M: int | None = None, *, device="cpu", seed: int = 
             out["d_residual_out"] = torch.randn((M, H), generator=gen, device=device).to(
                 torch.bfloat16)
         return out
+    if w.kind == "rms_bf16":  # rms_norm_reference (bench.py:58-65) on bf16 rows
+        weight = _weight(H, gen, device)
+        if row_offset:
+            gen.manual_seed(seed * 1_000_003 + row_offset)
+        x = torch.randn((M, H), generator=gen, device=device).to(torch.bfloat16)
+        return {"x": x, "weight": weight, "eps": w.eps}
     if w.kind == "rms_f32":  # utils.py:38-59: randn x and weight, fp32
         if row_offset:
             gen.manual_seed(seed * 1_000_003 + row_offset)
