@@ -47,7 +47,10 @@ def _dequant(codes, scales, rows, K):
 @pytest.mark.parametrize("M,N,K", [(128, 128, 128), (256, 256, 512), (1000, 384, 7168),
                                    (77, 128, 2048), (2048, 1024, 4096),
                                    # enough tiles for 128 x 256 tiles
-                                   (4800, 8192, 512), (4097, 9216, 384)])
+                                   (4800, 8192, 512), (4097, 9216, 384),
+                                   # decode batches: one tile row, mostly zero-filled
+                                   (1, 5120, 5120), (8, 1024, 2048), (32, 384, 7168),
+                                   (17, 256, 512), (33, 256, 1024)])
 def test_mxfp8_gemm_matches_dequantized_product(M, N, K):
     qa, sa, qb, sb = _operands(M, N, K, seed=M + N + K)
     d = mxfp8_gemm(qa, sa, qb, sb)
@@ -62,7 +65,8 @@ def test_mxfp8_gemm_matches_dequantized_product(M, N, K):
     assert bool((err <= bound).all()), f"max excess {(err - bound).max().item():.3e}"
 
 
-@pytest.mark.parametrize("M,N,K", [(256, 256, 1024), (1000, 512, 7168), (4736, 8192, 1024)])
+@pytest.mark.parametrize("M,N,K", [(256, 256, 1024), (1000, 512, 7168), (4736, 8192, 1024),
+                                   (8, 5120, 5120), (32, 1024, 4096)])
 def test_mxfp8_gemm_matches_cublas(M, N, K):
     qa, sa, qb, sb = _operands(M, N, K, seed=7 * M + K)
     d = mxfp8_gemm(qa, sa, qb, sb)
