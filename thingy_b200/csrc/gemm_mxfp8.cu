@@ -32,7 +32,8 @@
 //    (tcgen05.ld 32x32b, 32 columns at a time), rounds to bf16 and stores.
 // Tensor memory: the BN accumulator columns, then the scale columns of the 4
 // stages (256 or 512 columns allocated by warp 2, freed by it at the end).
-// No cluster, no multicast.
+// No cluster, no multicast. Batches of at most 32 rows take the decode kernel
+// below instead (swapped operands, K split over a cluster).
 //
 // Every wait is bounded (kWaitLimitCycles): a wait that gives up sets the
 // CTA's abort flag and the device error word; the producer stops issuing and
@@ -217,6 +218,223 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (warp == 2) tc::tmem_dealloc(tmem, P::kTmemCols);
 }
 
+// ---------------------------------------------------------------- decode
+//
+// Batches of at most 32 rows: the weight is the 128-row M side of the MMA and
+// the batch the 32-wide N side (D^T = B A^T), so a CTA streams 16 KB of
+// weight a K block with a 4 KB batch box (rows past M zero-filled) instead of
+// a 16 KB A box that is nearly all zero. The grid has only N / 128 tiles, so
+// K is split over a cluster of S CTAs (grid z) to put more SMs on the weight
+// stream; every rank accumulates its K range in its own tensor memory, the
+// non-leader ranks store their partial tiles into the leader's shared memory
+// (distributed shared memory, no multicast), and the leader adds them in rank
+// order, so the result does not depend on timing. Three K blocks share one
+// ring stage and one pair of barriers: at decode sizes the per-stage
+// hand-off, not the bytes, set the time of one-block stages.
+constexpr int kDecodeRows = 32;  // batch rows an MMA covers (its N)
+constexpr int kDecodeStages = 3;
+constexpr int kDecodeBlocks = 3;  // K blocks a stage
+constexpr int kDecodeMaxSplit = 8;
+
+struct DecodePlan {
+  static constexpr uint32_t kOffA = kTileBytes;  // batch box: 32 rows x 128 bytes
+  static constexpr uint32_t kOffSfW = kOffA + kDecodeRows * kBK;
+  static constexpr uint32_t kOffSfA = kOffSfW + kSfBytes;
+  static constexpr uint32_t kBlockBytes = (kOffSfA + kSfBytes + 1023u) & ~1023u;  // 21 KB
+  static constexpr uint32_t kStageBytes = kDecodeBlocks * kBlockBytes;
+  static constexpr size_t kSmemBytes = kDecodeStages * kStageBytes + 1024;
+  static constexpr uint32_t kTxBytes = kTileBytes + kDecodeRows * kBK + 2 * kSfBytes;
+  // tensor memory: 32 accumulator columns, then 8 scale columns a block slot
+  static constexpr uint32_t kSfCol = kDecodeRows;
+  static constexpr uint32_t kTmemCols = 128;
+  // the leader's partial-tile buffer (after the ring is idle): [S - 1][32][128] fp32
+  static constexpr uint32_t kPartBytes = kDecodeRows * kBM * 4;
+  static_assert(kSfCol + 8 * kDecodeStages * kDecodeBlocks <= kTmemCols, "tensor memory columns");
+  static_assert((kDecodeMaxSplit - 1) * kPartBytes <= kDecodeStages * kStageBytes, "partials");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_mxfp8_decode_kernel(const __grid_constant__ CUtensorMap map_a,
+                             const __grid_constant__ CUtensorMap map_b, const uint8_t* sfa,
+                             const uint8_t* sfb, uint16_t* d, int64_t ldd, int M, int K) {
+  using P = DecodePlan;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t full_bar[kDecodeStages];
+  __shared__ __align__(8) uint64_t empty_bar[kDecodeStages];
+  __shared__ __align__(8) uint64_t acc_bar;
+  __shared__ uint32_t tmem_base_slot;
+  __shared__ uint32_t abort_flag;
+  __shared__ float peer_bad;  // the leader's: non-zero once a rank gave up
+  __shared__ uint32_t issued[kDecodeStages];
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const uint32_t base = (smem_addr(smem_raw) + 1023u) & ~1023u;
+  const int n0 = blockIdx.x * kBM;  // 128 columns of D = 128 rows of the weight
+  const int KB = K / kBK, S = (int)gridDim.z;
+  const uint32_t rank = tc::cluster_ctarank();  // = blockIdx.z: the cluster spans z
+  const int kb0 = (int)((int64_t)KB * rank / S), kb1 = (int)((int64_t)KB * (rank + 1) / S);
+  const int NS = (kb1 - kb0 + kDecodeBlocks - 1) / kDecodeBlocks;  // ring stages used
+  volatile uint32_t* abortp = &abort_flag;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kDecodeStages; ++s) {
+      mbar_init(smem_addr(&full_bar[s]), 1);
+      mbar_init(smem_addr(&empty_bar[s]), 1);
+      issued[s] = 0;
+    }
+    mbar_init(smem_addr(&acc_bar), 1);
+    abort_flag = 0;
+    peer_bad = 0.f;
+    mbar_init_fence();
+  }
+  if (warp == 2) tc::tmem_alloc(smem_addr(&tmem_base_slot), P::kTmemCols);
+  tc::fence_before();
+  __syncthreads();
+  tc::fence_after();
+  const uint32_t tmem = tmem_base_slot;
+  griddep_wait();
+  griddep_launch_dependents();
+
+  if (warp == 0 && lane == 0) {
+    for (int j = 0; j < NS; ++j) {
+      const int s = j % kDecodeStages;
+      const uint32_t use = (uint32_t)(j / kDecodeStages);
+      if (use > 0 && !wait_or_abort(smem_addr(&empty_bar[s]), (use - 1u) & 1u, abortp)) break;
+      const uint32_t bar = smem_addr(&full_bar[s]);
+      const int first = kb0 + j * kDecodeBlocks, nb = min(kDecodeBlocks, kb1 - first);
+      issued[s] = use + 1u;
+      mbar_arrive_expect_tx(bar, (uint32_t)nb * P::kTxBytes);
+      for (int i = 0; i < nb; ++i) {
+        const int kb = first + i;
+        const uint32_t st = base + (uint32_t)s * P::kStageBytes + (uint32_t)i * P::kBlockBytes;
+        tc::tma_load_2d(st, &map_b, kb * kBK, n0, bar);
+        tc::tma_load_2d(st + P::kOffA, &map_a, kb * kBK, 0, bar);  // zero past row M
+        bulk_g2s(st + P::kOffSfW, sfb + ((int64_t)blockIdx.x * KB + kb) * kSfBytes, kSfBytes,
+                 bar);
+        bulk_g2s(st + P::kOffSfA, sfa + (int64_t)kb * kSfBytes, kSfBytes, bar);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    for (int j = 0; j < NS; ++j) {
+      const int s = j % kDecodeStages;
+      const uint32_t use = (uint32_t)(j / kDecodeStages);
+      if (!wait_or_abort(smem_addr(&full_bar[s]), use & 1u, abortp)) break;
+      tc::fence_after();
+      const int first = kb0 + j * kDecodeBlocks, nb = min(kDecodeBlocks, kb1 - first);
+      for (int i = 0; i < nb; ++i) {
+        const uint32_t st = base + (uint32_t)s * P::kStageBytes + (uint32_t)i * P::kBlockBytes;
+        const uint32_t sfw_col = tmem + P::kSfCol + 8u * (uint32_t)(s * kDecodeBlocks + i);
+        const uint32_t sfa_col = sfw_col + 4u;
+        tc::copy_sf(sfw_col, smem_desc(st + P::kOffSfW, 0, 128, kLayoutNone));
+        tc::copy_sf(sfa_col, smem_desc(st + P::kOffSfA, 0, 128, kLayoutNone));
+#pragma unroll
+        for (int kk = 0; kk < kBK / 32; ++kk) {
+          const uint64_t wd = smem_desc(st + 32u * kk, 16, 1024, kLayoutSw128);
+          const uint64_t ad = smem_desc(st + P::kOffA + 32u * kk, 16, 1024, kLayoutSw128);
+          tc::mma_mxf8(tmem, wd, ad, tc::mxf8_idesc(kBM, kDecodeRows, (uint32_t)kk), sfw_col,
+                       sfa_col, (j | i | kk) != 0);
+        }
+      }
+      tc::commit(smem_addr(&empty_bar[s]));
+    }
+    tc::commit(smem_addr(&acc_bar));
+  }
+  __syncwarp();
+
+  // ---- this rank's partial tile: warp w holds D^T rows n0 + 32 w + lane, one
+  // column a batch row
+  const bool acc_ok = __all_sync(0xffffffffu, mbar_wait_bounded(smem_addr(&acc_bar), 0u,
+                                                                kWaitLimitCycles) &&
+                                                  *abortp == 0u);
+  if (!acc_ok) *abortp = 1u;
+  tc::fence_after();
+  uint32_t r[kDecodeRows];
+  if (acc_ok) tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16), r);
+  __syncthreads();
+  const bool ok = *abortp == 0u;  // the same in every thread after the barrier
+  if (!ok) {
+    if (threadIdx.x == 0) {
+      atomicCAS(&g_gemm_device_error, kDevErrNone, kDevErrBulkWaitTimeout);
+      // let the copies in flight land before other ranks write this ring
+      for (int s = 0; s < kDecodeStages; ++s)
+        if (issued[s] > 0)
+          mbar_wait_bounded(smem_addr(&full_bar[s]), (issued[s] - 1u) & 1u, kDrainLimitCycles);
+    }
+    __syncthreads();
+  }
+  // every rank's ring is idle past this barrier; the leader's becomes the
+  // partial-tile buffer [S - 1][32 batch rows][128 weight rows] fp32
+  tc::cluster_sync();
+  const int row = warp * 32 + lane;
+  if (rank != 0) {
+    if (ok) {
+      const uint32_t dst = tc::mapa(base, 0) + (rank - 1u) * P::kPartBytes + (uint32_t)row * 4u;
+#pragma unroll
+      for (int m = 0; m < kDecodeRows; ++m)
+        if (m < M) tc::st_cluster_f32(dst + (uint32_t)(m * kBM * 4), __uint_as_float(r[m]));
+    } else if (threadIdx.x == 0) {
+      tc::st_cluster_f32(tc::mapa(smem_addr(&peer_bad), 0), 1.f);
+    }
+  }
+  tc::cluster_sync();
+  if (rank == 0 && ok && peer_bad == 0.f) {
+    const float* part = reinterpret_cast<const float*>(smem_raw + (base - smem_addr(smem_raw)));
+    uint16_t* dp = d + n0 + row;
+#pragma unroll
+    for (int m = 0; m < kDecodeRows; ++m) {
+      if (m < M) {
+        float v = __uint_as_float(r[m]);
+        for (int q = 1; q < S; ++q)  // rank order: the sum does not depend on timing
+          v += part[(q - 1) * (kDecodeRows * kBM) + m * kBM + row];
+        dp[(int64_t)m * ldd] = (uint16_t)(f2_to_bf2(make_float2(v, 0.f)) & 0xffffu);
+      }
+    }
+  }
+  if (rank == 0 && threadIdx.x == 0 && peer_bad != 0.f)
+    atomicCAS(&g_gemm_device_error, kDevErrNone, kDevErrBulkWaitTimeout);
+  tc::fence_before();
+  __syncthreads();
+  if (warp == 2) tc::tmem_dealloc(tmem, P::kTmemCols);
+}
+
+// Ranks a tile's K range is split over: enough CTAs for the SMs, at most 8 (a
+// portable cluster), at least one K block a rank.
+int decode_splits(int64_t N, int64_t K) {
+  const int64_t tiles = N / kBM, kb = K / kBK;
+  int64_t s = device_sm_count() / tiles;
+  if (s > kDecodeMaxSplit) s = kDecodeMaxSplit;
+  if (s > kb) s = kb;
+  return s < 1 ? 1 : (int)s;
+}
+
+cudaError_t launch_decode(const CUtensorMap& map_a, const CUtensorMap& map_b, const void* a_scale,
+                          const void* b_scale, void* d, int64_t ldd, int64_t M, int64_t N,
+                          int64_t K, cudaStream_t stream) {
+  auto kernel = gemm_mxfp8_decode_kernel;
+  const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)DecodePlan::kSmemBytes);
+  if (e != cudaSuccess) return e;
+  const int S = decode_splits(N, K);
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3((unsigned)(N / kBM), 1, (unsigned)S);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = DecodePlan::kSmemBytes;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[2];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  attr[1].id = cudaLaunchAttributeClusterDimension;
+  attr[1].val.clusterDim.x = 1;
+  attr[1].val.clusterDim.y = 1;
+  attr[1].val.clusterDim.z = (unsigned)S;
+  cfg.attrs = attr;
+  cfg.numAttrs = 2;
+  return cudaLaunchKernelEx(&cfg, kernel, map_a, map_b, static_cast<const uint8_t*>(a_scale),
+                            static_cast<const uint8_t*>(b_scale), static_cast<uint16_t*>(d), ldd,
+                            (int)M, (int)K);
+}
+
 template <int BN>
 cudaError_t launch_gemm(const CUtensorMap& map_a, const CUtensorMap& map_b, const void* a_scale,
                         const void* b_scale, void* d, int64_t ldd, int64_t M, int64_t N,
@@ -259,19 +477,21 @@ cudaError_t device_error_gemm(int* out, bool clear) {
 int gemm_mxfp8(const void* a, int64_t lda, const void* a_scale, const void* b, int64_t ldb,
                const void* b_scale, void* d, int64_t ldd, int64_t M, int64_t N, int64_t K,
                cudaStream_t stream, const char** why) {
+  const bool decode = M <= kDecodeRows;
   CUtensorMap map_a, map_b;
-  if (!tc::encode_e4m3_operand(&map_a, a, M, K, lda) ||
+  if (!tc::encode_e4m3_operand(&map_a, a, M, K, lda, decode ? kDecodeRows : kBM) ||
       !tc::encode_e4m3_operand(&map_b, b, N, K, ldb)) {
     *why = "cuTensorMapEncodeTiled failed for an operand";
     return CUTIE_ERR_CUDA;
   }
+  // decode batches: swapped operands, K split over a cluster. Otherwise
   // 256-wide tiles when N allows them and there are still enough of them to
-  // give every SM one; otherwise (decode batches, narrow N) 128-wide tiles,
-  // twice as many CTAs
+  // give every SM one, else 128-wide tiles, twice as many CTAs
   const bool wide = N % 256 == 0 && (N / 256) * ((M + kBM - 1) / kBM) >= device_sm_count();
   const cudaError_t e =
-      wide ? launch_gemm<256>(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K, stream)
-           : launch_gemm<128>(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K, stream);
+      decode ? launch_decode(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K, stream)
+      : wide ? launch_gemm<256>(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K, stream)
+             : launch_gemm<128>(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K, stream);
   if (e != cudaSuccess) {
     *why = cudaGetErrorString(e);
     return CUTIE_ERR_CUDA;

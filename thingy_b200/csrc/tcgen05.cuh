@@ -204,15 +204,15 @@ inline PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   return fn;
 }
 
-// A [rows, K] e4m3 operand, K contiguous, `ld` bytes between rows: 128 x 128
-// boxes, 128-byte swizzle, zero fill past the last row.
+// A [rows, K] e4m3 operand, K contiguous, `ld` bytes between rows: boxes of
+// 128 K bytes x box_rows rows, 128-byte swizzle, zero fill past the last row.
 inline bool encode_e4m3_operand(CUtensorMap* map, const void* ptr, int64_t rows, int64_t K,
-                                int64_t ld) {
+                                int64_t ld, int box_rows = 128) {
   auto fn = encode_fn();
   if (fn == nullptr) return false;
   const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)rows};
   const cuuint64_t strides[1] = {(cuuint64_t)ld};
-  const cuuint32_t box[2] = {128, 128};
+  const cuuint32_t box[2] = {128, (cuuint32_t)box_rows};
   const cuuint32_t estr[2] = {1, 1};
   return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box,
             estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
