@@ -109,6 +109,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t* abortp = &abort_flag;
 
   if (threadIdx.x == 0) {
+    tc::prefetch_map(&map_a);
+    tc::prefetch_map(&map_b);
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_addr(&full_bar[s]), 1);
       mbar_init(smem_addr(&empty_bar[s]), 1);
@@ -278,6 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t* abortp = &abort_flag;
 
   if (threadIdx.x == 0) {
+    tc::prefetch_map(&map_a);
+    tc::prefetch_map(&map_b);
     for (int s = 0; s < kDecodeStages; ++s) {
       mbar_init(smem_addr(&full_bar[s]), 1);
       mbar_init(smem_addr(&empty_bar[s]), 1);

@@ -27,6 +27,8 @@
 //    partial sum into every CTA of the cluster (distributed shared memory).
 //    After a cluster barrier every CTA adds the S partials in rank order:
 //    the same inv_rms bits everywhere.
+//    The x loads are issued before the first weight tiles, so that pass 1
+//    does not queue behind the weight ring.
 //  * pass 2: quantizing warp w makes the A tile of every 4th K block
 //    (normalise, 1x32 maxima, e8m0 scales, e4m3 codes into a K-major
 //    128-byte-swizzled A stage and its 512-byte scale atom), so four K blocks
@@ -73,6 +75,7 @@ constexpr int kThreads = 7 * 32;
 constexpr uint32_t kTmemCols = 256;
 constexpr uint32_t kAccCol = 0, kSfCol = 128;  // K block i: kSfCol + 8 (i % 4) (A), + 4 (B)
 constexpr int kBarProducers = 1;               // named barrier of the quantizing warps
+constexpr int kBarStreams = 2;                 // x warp -> weight warp: first x loads issued
 constexpr int kMaxSplits = 8;
 
 struct ProArgs {
@@ -185,6 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   volatile uint32_t* abortp = &abort_flag;
 
   if (threadIdx.x == 0) {
+    tc::prefetch_map(&map_x);
+    tc::prefetch_map(&map_b);
     for (int s = 0; s < kSA; ++s) {
       mbar_init(smem_addr(&full_a[s]), 1);
       mbar_init(smem_addr(&empty_a[s]), 1);
@@ -219,10 +224,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   // first (they have no part in pass 1) and wait on it after streaming
   if (warp == kWarpX) {
     tc::cluster_arrive();
-    if (lane == 0) {
-      // x iterations 0 .. kbs-1 feed pass 1, kbs .. 2 kbs-1 pass 2 (a
-      // resident ring keeps pass 1's stages for pass 2: kbs iterations)
-      for (int it = 0; it < x_iters; ++it) {
+    // x iterations 0 .. kbs-1 feed pass 1, kbs .. 2 kbs-1 pass 2 (a resident
+    // ring keeps pass 1's stages for pass 2: kbs iterations). The first XS
+    // need no wait; the weight stream starts once they are issued, so that
+    // pass 1's rows are not queued behind a ring of weight tiles.
+    const int x_first = x_iters < XS ? x_iters : XS;
+    auto issue_x = [&](int it_begin, int it_end) {
+      for (int it = it_begin; it < it_end; ++it) {
         const int xs = it % XS;
         if (it >= XS &&
             !mbar_wait_abortable(smem_addr(&x_empty[xs]), (uint32_t)(it / XS - 1) & 1u, abortp,
@@ -237,11 +245,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                           &map_x, 0, 2 * kb, (int)(m0 + 32 * q), bar);
         bulk_g2s(base + P::kOffW + 256u * (uint32_t)xs, a.w + kb * kTK, 256u, bar);
       }
-    }
+    };
+    if (lane == 0) issue_x(0, x_first);
+    __syncwarp();
+    asm volatile("bar.arrive %0, %1;" ::"n"(kBarStreams), "n"(64) : "memory");
+    if (lane == 0) issue_x(x_first, x_iters);
     __syncwarp();
     tc::cluster_wait();
   } else if (warp == kWarpB) {
     tc::cluster_arrive();
+    asm volatile("bar.sync %0, %1;" ::"n"(kBarStreams), "n"(64) : "memory");
     if (lane == 0) {
       for (int i = 0; i < kbs; ++i) {
         const int s = i % P::SB;
