@@ -93,6 +93,11 @@ SHAPES = [
     (2100, 1280, 512),
     (20, 2048, 3072),
     (1, 16384, 16384),
+    # at most 16 rows with every K block of a CTA resident (A made in place of
+    # x, one release for the MMAs), and 16 rows that are not resident
+    (13, 1024, 2048),
+    (16, 5120, 5120),
+    (16, 128, 16384),
 ]
 
 
@@ -129,6 +134,7 @@ def test_exact_sum_inputs_bit_exact(M, N, K):
 @pytest.mark.parametrize("M,N,K,kind", [
     (1, 5120, 5120, "student_t"), (8, 5120, 5120, "student_t"), (32, 5120, 5120, "student_t"),
     (128, 5120, 5120, "student_t"), (777, 1024, 7168, "normal"), (256, 640, 2048, "normal"),
+    (16, 5120, 5120, "student_t"), (3, 2048, 7168, "normal"),
 ])
 def test_random_inputs_within_contract(M, N, K, kind):
     x, w = _inputs(M, K, seed=7 * M + K, kind=kind)

@@ -100,27 +100,43 @@ struct ProArgs {
 // (xr = 32, or M rounded up to 8 when M < 32) x 128 bf16 columns, so a
 // decode batch's stages are small and the ring holds up to kMaxXS of them.
 constexpr int kMaxXS = 16;
-template <int QB>
+constexpr uint32_t kStaticSmem = 5376;  // the kernel's __shared__ arrays (ptxas: at most 5.2 KB)
+// SM (small): a block of at most 16 rows whose every K block has an x stage
+// of its own. Pass 2 then writes each K block's A tile over its x stage (the
+// 16-row A tile is no larger than the stage), the whole A operand of the CTA
+// is resident before the first MMA, and the K loop has no A hand-offs: the
+// weight is the MMA's 128-row M side, the block's rows its N = 16 side, and
+// the weight ring runs in stages of three K blocks with one barrier pair
+// each. (A K loop with one A stage a warp and a barrier hand-off for every K
+// block ran at about 0.44 us a block; the stand-alone decode GEMM, with no
+// A hand-offs, at about 0.29.)
+template <int QB, bool SM = false>
 struct Plan {
-  static constexpr uint32_t kXRegion = QB == 1 ? 32768u : QB == 3 ? 49152u : 65536u;
+  static_assert(!SM || QB == 1, "the small plan is for one 32-row quarter");
+  static constexpr uint32_t kXRegion = SM ? 61440u : QB == 1 ? 32768u : QB == 3 ? 49152u : 65536u;
   // one A stage per quantizing warp (two warps and a 9-stage weight ring
   // measured slower from 16 rows on, and no faster below)
   static constexpr int kSA = kMaxSA;
-  static constexpr int SB = QB == 1 ? 7 : QB == 3 ? 6 : 5;  // B ring stages
-  static constexpr uint32_t kOffA = 0;  // after the K loop: the fp32 partial rows
-  static constexpr uint32_t kOffSfA = kSA * kTile;
-  static constexpr uint32_t kOffW = kOffSfA + kSA * kAtom;  // kMaxXS chunks of 128 weights
-  static constexpr uint32_t kOffX = kOffW + kMaxXS * 256u;
-  static constexpr uint32_t kOffB = kOffX + kXRegion;
+  static constexpr int SB = SM ? 9 : QB == 1 ? 7 : QB == 3 ? 6 : 5;  // weight slots
+  static constexpr int BG = SM ? 3 : 1;  // K blocks a weight stage
+  static constexpr int NSB = SB / BG;    // weight stages
+  static_assert(SB % BG == 0, "whole stages");
+  static constexpr uint32_t kOffA = 0;  // A stages (SM: none, A is made over x)
+  static constexpr uint32_t kOffSfA = SM ? kXRegion + kMaxXS * 256u : kSA * kTile;
+  static constexpr uint32_t kOffW = SM ? kXRegion : kOffSfA + kSA * kAtom;  // chunks of 128 weights
+  static constexpr uint32_t kOffX = SM ? 0u : kOffW + kMaxXS * 256u;
+  static constexpr uint32_t kOffB = SM ? kOffSfA + kMaxXS * kAtom : kOffX + kXRegion;
   static constexpr uint32_t kOffSfB = kOffB + SB * kTile;
   static constexpr uint32_t kBytes = kOffSfB + SB * kAtom;
   static constexpr size_t kSmem = kBytes + 1024;  // + alignment of the base to 1 KB
-  // the other CTAs' partial tiles (rows with data) fit below kOffSfB
-  static constexpr uint32_t kPushArea = kOffSfB;
+  // after the K loop: the other CTAs' partial tiles (rows with data) fit below
+  // kOffSfB (SM: in the x region)
+  static constexpr uint32_t kPushArea = SM ? kXRegion : kOffSfB;
   // the partial rows (32 QB of them, 512 bytes each) fit the A stages
   static_assert(kSA * kTile >= 32u * QB * kTN * 4, "the partial tile fits the A stages");
+  static_assert(!SM || (kMaxSplits - 1) * 16u * kTN * 4u <= kPushArea, "SM partials fit");
   static_assert(kOffX % 1024 == 0 && kOffB % 1024 == 0, "swizzled tiles on 1 KB boundaries");
-  static_assert(kSmem + 6 * 1024 <= 227 * 1024, "shared memory (with the static arrays)");
+  static_assert(kSmem + kStaticSmem <= 227 * 1024, "shared memory (with the static arrays)");
 };
 
 __device__ __forceinline__ void st_smem_u8(uint32_t addr, uint32_t v) {
@@ -142,11 +158,11 @@ __device__ __forceinline__ uint32_t part_off(int row, int c4, int rows) {
   return ((uint32_t)c4 * (uint32_t)rows + (uint32_t)row) * 16u;
 }
 
-template <int QB>
+template <int QB, bool SM>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_rmsnorm_mxfp8_kernel(const __grid_constant__ CUtensorMap map_x,
                               const __grid_constant__ CUtensorMap map_b, const ProArgs a) {
-  using P = Plan<QB>;
+  using P = Plan<QB, SM>;
   extern __shared__ uint8_t smem_raw[];
   constexpr int kSA = P::kSA;
   __shared__ __align__(8) uint64_t full_a[kMaxSA], empty_a[kMaxSA];
@@ -206,7 +222,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // pass 1: each quantizing warp arrives; pass 2: the one warp, with count 4
     for (int s = 0; s < kMaxXS; ++s) mbar_init(smem_addr(&x_empty[s]), kProducerWarps);
     mbar_init(smem_addr(&acc_bar), 1);
-    abort_flag = 0;
+    // the small plan needs every K block resident (the host only picks it then)
+    abort_flag = SM && !resident ? 1u : 0u;
     mbar_init_fence();
   }
   if (warp == kWarpMma) tc::tmem_alloc(smem_addr(&tmem_slot), kTmemCols);
@@ -256,18 +273,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::cluster_arrive();
     asm volatile("bar.sync %0, %1;" ::"n"(kBarStreams), "n"(64) : "memory");
     if (lane == 0) {
-      for (int i = 0; i < kbs; ++i) {
-        const int s = i % P::SB;
-        if (i >= P::SB &&
-            !mbar_wait_abortable(smem_addr(&empty_b[s]), (uint32_t)(i / P::SB - 1) & 1u, abortp,
+      // stage j holds K blocks BG j .. BG j + BG - 1 in slots BG (j % NSB) + ...
+      const int nst = (kbs + P::BG - 1) / P::BG;
+      for (int j = 0; j < nst; ++j) {
+        const int s = j % P::NSB;
+        if (j >= P::NSB &&
+            !mbar_wait_abortable(smem_addr(&empty_b[s]), (uint32_t)(j / P::NSB - 1) & 1u, abortp,
                                  a.wait_limit))
           break;
+        const int first = j * P::BG, nb = min(P::BG, kbs - first);
         const uint32_t bar = smem_addr(&full_b[s]);
-        issued_b[s] = (uint32_t)(i / P::SB) + 1u;
-        mbar_arrive_expect_tx(bar, kTile + kAtom);
-        tc::tma_load_2d(base + P::kOffB + (uint32_t)s * kTile, &map_b, (kb0 + i) * kTK, n0, bar);
-        bulk_g2s(base + P::kOffSfB + (uint32_t)s * kAtom,
-                 a.sfb + ((int64_t)blockIdx.x * KB + kb0 + i) * kAtom, kAtom, bar);
+        issued_b[s] = (uint32_t)(j / P::NSB) + 1u;
+        mbar_arrive_expect_tx(bar, (uint32_t)nb * (kTile + kAtom));
+        for (int i = 0; i < nb; ++i) {
+          const uint32_t slot = (uint32_t)(s * P::BG + i);
+          const int kb = kb0 + first + i;
+          tc::tma_load_2d(base + P::kOffB + slot * kTile, &map_b, kb * kTK, n0, bar);
+          bulk_g2s(base + P::kOffSfB + slot * kAtom, a.sfb + ((int64_t)blockIdx.x * KB + kb) * kAtom,
+                   kAtom, bar);
+        }
       }
     }
     __syncwarp();
@@ -275,7 +299,41 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == kWarpMma) {
     tc::cluster_arrive();  // the MMAs wait for A tiles, which come after pass 1
     tc::cluster_wait();
-    if (lane == 0) {
+    if constexpr (SM) {
+      // the whole A operand is made before the first MMA (full_a[0] once)
+      if (lane == 0 && mbar_wait_abortable(smem_addr(&full_a[0]), 0u, abortp, a.wait_limit)) {
+        const int nst = (kbs + P::BG - 1) / P::BG;
+        for (int j = 0; j < nst; ++j) {
+          const int s = j % P::NSB;
+          if (!mbar_wait_abortable(smem_addr(&full_b[s]), (uint32_t)(j / P::NSB) & 1u, abortp,
+                                   a.wait_limit))
+            break;
+          tc::fence_after();
+          const int first = j * P::BG, nb = min(P::BG, kbs - first);
+          for (int i = 0; i < nb; ++i) {
+            const int blk = first + i;  // this CTA's K block: x (now A) stage blk
+            const uint32_t slot = (uint32_t)(s * P::BG + i);
+            const uint32_t sfa_col = tmem + kSfCol + 8u * slot, sfb_col = sfa_col + 4u;
+            tc::copy_sf(sfa_col, tc::smem_desc(base + P::kOffSfA + (uint32_t)blk * kAtom, 0, 128,
+                                               tc::kLayoutNone));
+            tc::copy_sf(sfb_col, tc::smem_desc(base + P::kOffSfB + slot * kAtom, 0, 128,
+                                               tc::kLayoutNone));
+#pragma unroll
+            for (int kk = 0; kk < kTK / 32; ++kk) {
+              const uint64_t ad = tc::smem_desc(base + P::kOffX + (uint32_t)blk * xstage + 32u * kk,
+                                                16, 1024, tc::kLayoutSw128);
+              const uint64_t bd = tc::smem_desc(base + P::kOffB + slot * kTile + 32u * kk, 16, 1024,
+                                                tc::kLayoutSw128);
+              // D^T: 128 weight rows x 16 block rows
+              tc::mma_mxf8(tmem + kAccCol, bd, ad, tc::mxf8_idesc(kTN, 16, (uint32_t)kk), sfb_col,
+                           sfa_col, (blk | kk) != 0);
+            }
+          }
+          tc::commit(smem_addr(&empty_b[s]));  // the weight stage is free after its MMAs
+        }
+      }
+      if (lane == 0) tc::commit(smem_addr(&acc_bar));  // final (or, on abort, quiet)
+    } else if (lane == 0) {
       for (int i = 0; i < kbs; ++i) {
         const int sa = i % kSA, sb = i % P::SB;
         if (!mbar_wait_abortable(smem_addr(&full_a[sa]), (uint32_t)(i / kSA) & 1u, abortp,
@@ -400,12 +458,46 @@ __global__ void __launch_bounds__(kThreads, 1)
       // ---- pass 2: warp w < kSA makes the A tiles of this CTA's K blocks
       // w, w + kSA, ... (x_full slot it % 4 then always belongs to one warp)
       const bool store_q = a.q != nullptr && blockIdx.x == 0;  // one tile column writes q
-      for (int i = warp; warp < kSA && i < kbs; i += kSA) {
+      // normalise, quantize and store chunk j of tile row m of K block kb
+      auto finish_item = [&](uint32_t(&v)[8], const uint32_t(&wv)[8], uint32_t a_st,
+                             uint32_t sf_st, int kb, int m) {
+        const float iv = m < Mr ? inv_s[m] : 0.f;
+        const float2 inv2 = make_float2(iv, iv);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          v[k] = mul_bf2(f2_to_bf2(__fmul2_rn(bf2_to_f2(v[k]), inv2)), wv[k]);
+        // 1x32 group = this chunk and its neighbour (lane ^ 1)
+        uint32_t am = absmax_bf2(absmax_bf2(absmax_bf2(v[0], v[1]), absmax_bf2(v[2], v[3])),
+                                 absmax_bf2(absmax_bf2(v[4], v[5]), absmax_bf2(v[6], v[7])));
+        am &= 0x7fff7fffu;
+        am = max_bf2(am, am >> 16);
+        am = max_bf2(am, __shfl_xor_sync(0xffffffffu, am, 1)) & 0xffffu;
+        const float sc = make_scale(__uint_as_float(am << 16), true);
+        const uint32_t e8 = __float_as_uint(sc) >> 23;
+        const float rc = __uint_as_float((254u << 23) - __float_as_uint(sc));  // exact
+        const float2 rc2 = make_float2(rc, rc);
+        uint32_t c4[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          c4[k] = f4_to_e4m3x4(__fmul2_rn(bf2_to_f2(v[2 * k]), rc2),
+                               __fmul2_rn(bf2_to_f2(v[2 * k + 1]), rc2));
+        if (m < Mr) {
+          // K-major, 128-byte swizzled A tile: row m, 16-byte chunk j at j ^ (m % 8)
+          st_smem(a_st + (uint32_t)m * 128u + (((uint32_t)j ^ ((uint32_t)m & 7u)) << 4), c4);
+          if ((j & 1) == 0)
+            st_smem_u8(sf_st + (uint32_t)((m & 31) * 16 + (m >> 5) * 4 + (j >> 1)), e8);
+          if (store_q) {
+            st_stream(a.q + (m0 + m) * a.ldq + kb * kTK + 16 * j, c4);
+            if ((j & 1) == 0) a.qs[swizzled_offset(m0 + m, kb * 4 + (j >> 1), KB)] = (uint8_t)e8;
+          }
+        }
+      };
+      for (int i = warp; i < kbs; i += kSA) {
         const int it = kbs + i, kb = kb0 + i;
         const int sa = i % kSA, xs = resident ? i : it % XS;
         bool ok = resident || mbar_wait_abortable(smem_addr(&x_full[xf(it)]), xp(it), abortp,
                                                   a.wait_limit);
-        if (ok && i >= kSA)
+        if (!SM && ok && i >= kSA)
           ok = mbar_wait_abortable(smem_addr(&empty_a[sa]), (uint32_t)(i / kSA - 1) & 1u, abortp,
                                    a.wait_limit);
         if (!__all_sync(0xffffffffu, ok)) {  // the warp acts as one
@@ -415,49 +507,23 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t w_st = base + P::kOffW + 256u * (uint32_t)xs + 32u * (uint32_t)j;
         const uint4 w0 = ld_smem(w_st), w1 = ld_smem(w_st + 16u);
         const uint32_t wv[8] = {w0.x, w0.y, w0.z, w0.w, w1.x, w1.y, w1.z, w1.w};
-        const uint32_t a_st = base + P::kOffA + (uint32_t)sa * kTile;
-        const uint32_t sf_st = base + P::kOffSfA + (uint32_t)sa * kAtom;
         const uint32_t x_st = base + P::kOffX + (uint32_t)xs * xstage;
+        // SM: the A tile goes over its own x stage (row m writes 128 bytes at
+        // 128 m, over x lines that rows before m / 2 + 1 held: those rows have
+        // been read, by this warp, in this or an earlier step of the loop below)
+        const uint32_t a_st = SM ? x_st : base + P::kOffA + (uint32_t)sa * kTile;
+        const uint32_t sf_st = base + P::kOffSfA + (uint32_t)(SM ? i : sa) * kAtom;
 #pragma unroll 2
         for (int r = 0; r < 8 * QB; ++r) {
           const int m = (lane >> 3) + 4 * r;  // tile row
           if (!__any_sync(0xffffffffu, m < Mr)) break;
           uint32_t v[8];
           load_chunk(x_st, m, v);
-          const float iv = m < Mr ? inv_s[m] : 0.f;
-          const float2 inv2 = make_float2(iv, iv);
-#pragma unroll
-          for (int k = 0; k < 8; ++k)
-            v[k] = mul_bf2(f2_to_bf2(__fmul2_rn(bf2_to_f2(v[k]), inv2)), wv[k]);
-          // 1x32 group = this chunk and its neighbour (lane ^ 1)
-          uint32_t am = absmax_bf2(absmax_bf2(absmax_bf2(v[0], v[1]), absmax_bf2(v[2], v[3])),
-                                   absmax_bf2(absmax_bf2(v[4], v[5]), absmax_bf2(v[6], v[7])));
-          am &= 0x7fff7fffu;
-          am = max_bf2(am, am >> 16);
-          am = max_bf2(am, __shfl_xor_sync(0xffffffffu, am, 1)) & 0xffffu;
-          const float sc = make_scale(__uint_as_float(am << 16), true);
-          const uint32_t e8 = __float_as_uint(sc) >> 23;
-          const float rc = __uint_as_float((254u << 23) - __float_as_uint(sc));  // exact
-          const float2 rc2 = make_float2(rc, rc);
-          uint32_t c4[4];
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            c4[k] = f4_to_e4m3x4(__fmul2_rn(bf2_to_f2(v[2 * k]), rc2),
-                                 __fmul2_rn(bf2_to_f2(v[2 * k + 1]), rc2));
-          if (m < Mr) {
-            // K-major, 128-byte swizzled A tile: row m, 16-byte chunk j at j ^ (m % 8)
-            st_smem(a_st + (uint32_t)m * 128u + (((uint32_t)j ^ ((uint32_t)m & 7u)) << 4), c4);
-            if ((j & 1) == 0)
-              st_smem_u8(sf_st + (uint32_t)((m & 31) * 16 + (m >> 5) * 4 + (j >> 1)), e8);
-            if (store_q) {
-              st_stream(a.q + (m0 + m) * a.ldq + kb * kTK + 16 * j, c4);
-              if ((j & 1) == 0) a.qs[swizzled_offset(m0 + m, kb * 4 + (j >> 1), KB)] = (uint8_t)e8;
-            }
-          }
+          finish_item(v, wv, a_st, sf_st, kb, m);
         }
-        tc::fence_async_smem();  // the A stage writes come before the MMAs
+        if constexpr (!SM) tc::fence_async_smem();  // the A stage writes come before the MMAs
         __syncwarp();
-        if (lane == 0) {
+        if (!SM && lane == 0) {
           if (!resident)  // counts for all four warps
             asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(
                              smem_addr(&x_empty[xs])),
@@ -465,6 +531,12 @@ __global__ void __launch_bounds__(kThreads, 1)
                          : "memory");
           mbar_arrive(smem_addr(&full_a[sa]));
         }
+      }
+      if constexpr (SM) {
+        tc::fence_async_smem();  // this thread's A tile writes come before the MMAs
+        // every A tile of this CTA is made: one release for the MMAs
+        asm volatile("bar.sync %0, %1;" ::"n"(kBarProducers), "n"(kProducers) : "memory");
+        if (t == 0) mbar_arrive(smem_addr(&full_a[0]));
       }
       // the scale rows of the padding past M in the last block (this CTA's K
       // blocks), zero in q_scale
@@ -484,75 +556,110 @@ __global__ void __launch_bounds__(kThreads, 1)
                                          *abortp == 0u);
     tc::fence_after();
   }
-  const int row = warp * 32 + lane;  // tile row of this thread (warps 0-3)
-  const bool row_live = warp < kProducerWarps && row < Mr;
-  const uint32_t tm_row = tmem + ((uint32_t)(warp * 32) << 16) + kAccCol;
-  // Push: the others store their rows with data straight into the leader's
-  // shared memory (remote stores, no round trip) once every CTA's MMAs are
-  // done; pull, when they do not fit: each keeps its rows and the leader
-  // reads them. Both use two cluster barriers.
-  const bool push = (uint32_t)(S - 1) * (uint32_t)Mr * 512u <= P::kPushArea;
-  // slot of rank p's partial rows in the leader: column groups outermost
-  auto push_off = [&](int p, int rw, int c4) {
-    return (uint32_t)(p - 1) * (uint32_t)Mr * 512u + ((uint32_t)c4 * (uint32_t)Mr + (uint32_t)rw) * 16u;
-  };
-  if (S > 1) {
-    if (push) tc::cluster_sync();  // every CTA's MMAs are done: the leader's memory is free
-    if (rank > 0 && acc_ok && __any_sync(0xffffffffu, row_live)) {
-      for (int c = 0; c < kTN; c += 32) {
-        uint32_t r[32];
-        tc::tmem_ld32(tm_row + (uint32_t)c, r);
-        if (row_live) {
+  if constexpr (SM) {
+    // D^T in tensor memory: warp w (< 4) holds weight rows n0 + 32 w + lane,
+    // one column a block row. Once every CTA's MMAs are done the others store
+    // their Mr columns into the leader's x region ([S - 1][Mr][128] fp32);
+    // the leader adds them to its own in rank order and stores D.
+    const int n = warp * 32 + lane;  // weight row of the tile = column of D
+    uint32_t r[32];
+    if (acc_ok) tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + kAccCol, r);
+    if (S > 1) {
+      tc::cluster_sync();  // every CTA's MMAs are done: the leader's memory is free
+      if (rank > 0 && acc_ok) {
+        const uint32_t dst =
+            tc::mapa(base + P::kOffX + ((uint32_t)(rank - 1) * (uint32_t)Mr * kTN + (uint32_t)n) * 4u,
+                     0u);
 #pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint32_t v4[4] = {r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]};
-            if (push) {
-              const uint32_t dst = tc::mapa(base + push_off(rank, row, c / 4 + k), 0u);
-              asm volatile("st.shared::cluster.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst),
-                           "r"(v4[0]), "r"(v4[1]), "r"(v4[2]), "r"(v4[3])
-                           : "memory");
-            } else {
-              st_smem(base + P::kOffA + part_off(row, c / 4 + k, Mr), v4);
+        for (int m = 0; m < 16; ++m)
+          if (m < Mr) tc::st_cluster_f32(dst + (uint32_t)(m * kTN * 4), __uint_as_float(r[m]));
+      }
+      tc::cluster_sync();  // every partial is in place
+    }
+    if ((S == 1 || rank == 0) && acc_ok) {
+      const float* part_t =
+          reinterpret_cast<const float*>(smem_raw + (base + P::kOffX - smem_addr(smem_raw)));
+#pragma unroll
+      for (int m = 0; m < 16; ++m) {
+        if (m < Mr) {
+          float v = __uint_as_float(r[m]);
+          for (int p = 1; p < S; ++p)  // the other CTAs' partials, in rank order
+            v = __fadd_rn(v, part_t[((p - 1) * Mr + m) * kTN + n]);
+          a.d[(m0 + m) * a.ldd + n0 + n] = (uint16_t)(f2_to_bf2(make_float2(v, 0.f)) & 0xffffu);
+        }
+      }
+    }
+  } else {
+    const int row = warp * 32 + lane;  // tile row of this thread (warps 0-3)
+    const bool row_live = warp < kProducerWarps && row < Mr;
+    const uint32_t tm_row = tmem + ((uint32_t)(warp * 32) << 16) + kAccCol;
+    // Push: the others store their rows with data straight into the leader's
+    // shared memory (remote stores, no round trip) once every CTA's MMAs are
+    // done; pull, when they do not fit: each keeps its rows and the leader
+    // reads them. Both use two cluster barriers.
+    const bool push = (uint32_t)(S - 1) * (uint32_t)Mr * 512u <= P::kPushArea;
+    // slot of rank p's partial rows in the leader: column groups outermost
+    auto push_off = [&](int p, int rw, int c4) {
+      return (uint32_t)(p - 1) * (uint32_t)Mr * 512u + ((uint32_t)c4 * (uint32_t)Mr + (uint32_t)rw) * 16u;
+    };
+    if (S > 1) {
+      if (push) tc::cluster_sync();  // every CTA's MMAs are done: the leader's memory is free
+      if (rank > 0 && acc_ok && __any_sync(0xffffffffu, row_live)) {
+        for (int c = 0; c < kTN; c += 32) {
+          uint32_t r[32];
+          tc::tmem_ld32(tm_row + (uint32_t)c, r);
+          if (row_live) {
+  #pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint32_t v4[4] = {r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]};
+              if (push) {
+                const uint32_t dst = tc::mapa(base + push_off(rank, row, c / 4 + k), 0u);
+                asm volatile("st.shared::cluster.v4.u32 [%0], {%1,%2,%3,%4};" ::"r"(dst),
+                             "r"(v4[0]), "r"(v4[1]), "r"(v4[2]), "r"(v4[3])
+                             : "memory");
+              } else {
+                st_smem(base + P::kOffA + part_off(row, c / 4 + k, Mr), v4);
+              }
             }
           }
         }
       }
+      tc::cluster_sync();  // every partial tile is in place
     }
-    tc::cluster_sync();  // every partial tile is in place
-  }
-  if ((S == 1 || rank == 0) && acc_ok && __any_sync(0xffffffffu, row_live)) {
-    for (int c = 0; c < kTN; c += 32) {
-      uint32_t r[32];
-      tc::tmem_ld32(tm_row + (uint32_t)c, r);
-      if (row_live) {
-        for (int p = 1; p < S; ++p) {  // the other CTAs' partials, in rank order
-#pragma unroll
-          for (int k = 0; k < 8; ++k) {
-            const uint4 o =
-                push ? ld_smem(base + push_off(p, row, c / 4 + k))
-                     : ld_cluster_v4(tc::mapa(base + P::kOffA + part_off(row, c / 4 + k, Mr),
-                                              (uint32_t)p));
-            const uint32_t ov[4] = {o.x, o.y, o.z, o.w};
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              r[4 * k + e] =
-                  __float_as_uint(__fadd_rn(__uint_as_float(r[4 * k + e]), __uint_as_float(ov[e])));
+    if ((S == 1 || rank == 0) && acc_ok && __any_sync(0xffffffffu, row_live)) {
+      for (int c = 0; c < kTN; c += 32) {
+        uint32_t r[32];
+        tc::tmem_ld32(tm_row + (uint32_t)c, r);
+        if (row_live) {
+          for (int p = 1; p < S; ++p) {  // the other CTAs' partials, in rank order
+  #pragma unroll
+            for (int k = 0; k < 8; ++k) {
+              const uint4 o =
+                  push ? ld_smem(base + push_off(p, row, c / 4 + k))
+                       : ld_cluster_v4(tc::mapa(base + P::kOffA + part_off(row, c / 4 + k, Mr),
+                                                (uint32_t)p));
+              const uint32_t ov[4] = {o.x, o.y, o.z, o.w};
+  #pragma unroll
+              for (int e = 0; e < 4; ++e)
+                r[4 * k + e] =
+                    __float_as_uint(__fadd_rn(__uint_as_float(r[4 * k + e]), __uint_as_float(ov[e])));
+            }
           }
-        }
-        uint32_t o16[16];
-#pragma unroll
-        for (int k = 0; k < 16; ++k)
-          o16[k] = f2_to_bf2(make_float2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1])));
-        uint8_t* dp = reinterpret_cast<uint8_t*>(a.d + (m0 + row) * a.ldd + n0 + c);
-#pragma unroll
-        for (int k = 0; k < 4; ++k) {
-          const uint32_t vv[4] = {o16[4 * k], o16[4 * k + 1], o16[4 * k + 2], o16[4 * k + 3]};
-          st_stream(dp + 16 * k, vv);
+          uint32_t o16[16];
+  #pragma unroll
+          for (int k = 0; k < 16; ++k)
+            o16[k] = f2_to_bf2(make_float2(__uint_as_float(r[2 * k]), __uint_as_float(r[2 * k + 1])));
+          uint8_t* dp = reinterpret_cast<uint8_t*>(a.d + (m0 + row) * a.ldd + n0 + c);
+  #pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const uint32_t vv[4] = {o16[4 * k], o16[4 * k + 1], o16[4 * k + 2], o16[4 * k + 3]};
+            st_stream(dp + 16 * k, vv);
+          }
         }
       }
     }
+    if (S > 1 && !push) tc::cluster_sync();  // the leader has read every partial tile
   }
-  if (S > 1 && !push) tc::cluster_sync();  // the leader has read every partial tile
   tc::fence_before();
   __syncthreads();
   if (*abortp != 0u && threadIdx.x == 0) {
@@ -584,11 +691,11 @@ bool encode_x(CUtensorMap* map, const void* x, int64_t M, int64_t K, int64_t ldx
             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
-template <int QB>
+template <int QB, bool SM = false>
 cudaError_t launch_one(const CUtensorMap& map_x, const CUtensorMap& map_b, const ProArgs& a,
                        int64_t N, int64_t M, cudaStream_t stream) {
-  using P = Plan<QB>;
-  auto kernel = gemm_rmsnorm_mxfp8_kernel<QB>;
+  using P = Plan<QB, SM>;
+  auto kernel = gemm_rmsnorm_mxfp8_kernel<QB, SM>;
   const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              (int)P::kSmem);
   if (e != cudaSuccess) return e;
@@ -650,8 +757,14 @@ int gemm_rmsnorm_mxfp8(const void* x, int64_t ldx, const void* weight, float eps
   a.eps = eps;
   a.rcp_K = 1.0f / (float)K;
   a.wait_limit = wait_limit;
+  // the small plan: at most 16 rows, and every K block of a CTA resident in
+  // an x stage of its own
+  const int64_t kbs_max = (K / kTK + a.splits - 1) / a.splits;
+  const int64_t xs_small = Plan<1, true>::kXRegion / ((uint32_t)xr * 256u);
+  const bool small = M <= 16 && kbs_max <= (xs_small < kMaxXS ? xs_small : kMaxXS);
   cudaError_t e;
-  switch (M >= kTM ? 4 : (int)((M + 31) / 32)) {
+  switch (small ? 0 : M >= kTM ? 4 : (int)((M + 31) / 32)) {
+    case 0: e = launch_one<1, true>(map_x, map_b, a, N, M, stream); break;
     case 1: e = launch_one<1>(map_x, map_b, a, N, M, stream); break;
     case 2: e = launch_one<2>(map_x, map_b, a, N, M, stream); break;
     case 3: e = launch_one<3>(map_x, map_b, a, N, M, stream); break;
