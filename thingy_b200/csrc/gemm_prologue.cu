@@ -103,13 +103,13 @@ constexpr int kMaxXS = 16;
 constexpr uint32_t kStaticSmem = 5376;  // the kernel's __shared__ arrays (ptxas: at most 5.2 KB)
 // SM (small): a block of at most 16 rows whose every K block has an x stage
 // of its own. Pass 2 then writes each K block's A tile over its x stage (the
-// 16-row A tile is no larger than the stage), the whole A operand of the CTA
-// is resident before the first MMA, and the K loop has no A hand-offs: the
-// weight is the MMA's 128-row M side, the block's rows its N = 16 side, and
-// the weight ring runs in stages of three K blocks with one barrier pair
-// each. (A K loop with one A stage a warp and a barrier hand-off for every K
-// block ran at about 0.44 us a block; the stand-alone decode GEMM, with no
-// A hand-offs, at about 0.29.)
+// 16-row A tile is no larger than the stage), so A needs no ring: the A
+// tiles of three K blocks are released together, on one barrier, and the MMA
+// thread waits once for those and once for the weight stage of the same
+// three blocks. The weight is the MMA's 128-row M side and the block's rows
+// its N = 16 side. (A K loop with one A stage a warp and a barrier hand-off
+// for every K block ran at about 0.44 us a block; the stand-alone decode
+// GEMM, one hand-off a three-block stage, at about 0.29.)
 template <int QB, bool SM = false>
 struct Plan {
   static_assert(!SM || QB == 1, "the small plan is for one 32-row quarter");
@@ -175,6 +175,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   // ring may have fewer stages than there are warps. x_empty by x stage.
   __shared__ __align__(8) uint64_t x_full[kMaxXS], x_empty[kMaxXS];
   __shared__ __align__(8) uint64_t acc_bar;
+  // SM: A group g (K blocks 3 g .. 3 g + 2, the blocks of weight stage g) is
+  // made when each of its blocks' warps has arrived once
+  __shared__ __align__(8) uint64_t a_group[SM ? (kMaxXS + 2) / 3 : 1];
   __shared__ float part[kMaxSplits][kTM];  // row partial sums from every CTA of the cluster
   __shared__ float inv_s[kTM];             // inv_rms of the block's rows
   __shared__ uint32_t tmem_slot, abort_flag;
@@ -222,6 +225,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     // pass 1: each quantizing warp arrives; pass 2: the one warp, with count 4
     for (int s = 0; s < kMaxXS; ++s) mbar_init(smem_addr(&x_empty[s]), kProducerWarps);
     mbar_init(smem_addr(&acc_bar), 1);
+    if constexpr (SM)
+      for (int g = 0; g < (kMaxXS + 2) / 3; ++g)
+        mbar_init(smem_addr(&a_group[g]), (uint32_t)max(1, min(3, kbs - 3 * g)));
     // the small plan needs every K block resident (the host only picks it then)
     abort_flag = SM && !resident ? 1u : 0u;
     mbar_init_fence();
@@ -300,12 +306,13 @@ __global__ void __launch_bounds__(kThreads, 1)
     tc::cluster_arrive();  // the MMAs wait for A tiles, which come after pass 1
     tc::cluster_wait();
     if constexpr (SM) {
-      // the whole A operand is made before the first MMA (full_a[0] once)
-      if (lane == 0 && mbar_wait_abortable(smem_addr(&full_a[0]), 0u, abortp, a.wait_limit)) {
+      // stage j takes weight stage j and A group j (the same three K blocks)
+      if (lane == 0) {
         const int nst = (kbs + P::BG - 1) / P::BG;
         for (int j = 0; j < nst; ++j) {
           const int s = j % P::NSB;
-          if (!mbar_wait_abortable(smem_addr(&full_b[s]), (uint32_t)(j / P::NSB) & 1u, abortp,
+          if (!mbar_wait_abortable(smem_addr(&a_group[j]), 0u, abortp, a.wait_limit) ||
+              !mbar_wait_abortable(smem_addr(&full_b[s]), (uint32_t)(j / P::NSB) & 1u, abortp,
                                    a.wait_limit))
             break;
           tc::fence_after();
@@ -521,8 +528,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           load_chunk(x_st, m, v);
           finish_item(v, wv, a_st, sf_st, kb, m);
         }
-        if constexpr (!SM) tc::fence_async_smem();  // the A stage writes come before the MMAs
+        tc::fence_async_smem();  // the A stage writes come before the MMAs
         __syncwarp();
+        if (SM && lane == 0) mbar_arrive(smem_addr(&a_group[i / 3]));
         if (!SM && lane == 0) {
           if (!resident)  // counts for all four warps
             asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(
@@ -531,12 +539,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                          : "memory");
           mbar_arrive(smem_addr(&full_a[sa]));
         }
-      }
-      if constexpr (SM) {
-        tc::fence_async_smem();  // this thread's A tile writes come before the MMAs
-        // every A tile of this CTA is made: one release for the MMAs
-        asm volatile("bar.sync %0, %1;" ::"n"(kBarProducers), "n"(kProducers) : "memory");
-        if (t == 0) mbar_arrive(smem_addr(&full_a[0]));
       }
       // the scale rows of the padding past M in the last block (this CTA's K
       // blocks), zero in q_scale
