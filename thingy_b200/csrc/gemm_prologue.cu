@@ -180,6 +180,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t a_group[SM ? (kMaxXS + 2) / 3 : 1];
   __shared__ float part[kMaxSplits][kTM];  // row partial sums from every CTA of the cluster
   __shared__ float inv_s[kTM];             // inv_rms of the block's rows
+  __shared__ float gsum[16];               // SM: the 8-lane groups' sums of squares
   __shared__ uint32_t tmem_slot, abort_flag;
   __shared__ uint32_t issued_b[P::SB], issued_x[kMaxXS];
 
@@ -388,6 +389,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---- pass 1: this thread's share of the rows' sums of squares over this
     // CTA's K blocks: rows (t / 8) + 16 u, chunk j, every K block in order
     constexpr int U = 2 * QB;
+    const int Mp = Mr <= 1 ? 1 : Mr <= 2 ? 2 : Mr <= 4 ? 4 : Mr <= 8 ? 8 : 16;  // SM
     float2 acc[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) acc[u] = make_float2(0.f, 0.f);
@@ -413,6 +415,20 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!__all_sync(0xffffffffu, ok)) {
         *abortp = 1u;
         lost = true;
+      } else if constexpr (SM) {
+        // Mr <= 16: row m's K blocks are spread over the 16 / Mp groups of 8
+        // lanes g = m + Mp sub (Mp = Mr rounded up to a power of two), group
+        // sub taking blocks sub, sub + 16 / Mp, ...: all 128 threads add
+        const int g = t >> 3, m = g % Mp, R = 16 / Mp;
+        if (m < Mr) {
+#pragma unroll 4
+          for (int it = g / Mp; it < kbs; it += R) {
+            uint32_t v[8];
+            load_chunk(base + P::kOffX + (uint32_t)it * xstage, m, v);
+#pragma unroll
+            for (int k = 0; k < 8; ++k) sq_acc(acc[0], v[k]);
+          }
+        }
       } else {
 #pragma unroll 4
         for (int it = 0; it < kbs; ++it) add_squares(it);
@@ -435,7 +451,22 @@ __global__ void __launch_bounds__(kThreads, 1)
     // row partials: the 8 lanes of a row add their chunks (a symmetric
     // butterfly: all 8 get the same bits), then lane j of the row writes it
     // into part[rank][row] of CTA j (and j + 8) of the cluster
-    if (!failed) {
+    if (!failed && SM) {
+      // a group's 8 lanes add their chunks, then the groups of a row add in
+      // the order of their K blocks' residue (sub = 0, 1, ...), and thread m
+      // writes row m's partial into part[rank][m] of every CTA of the cluster
+      float v = __fadd_rn(acc[0].x, acc[0].y);
+      v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 1));
+      v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 2));
+      v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, 4));
+      if (j == 0) gsum[t >> 3] = v;
+      asm volatile("bar.sync %0, %1;" ::"n"(kBarProducers), "n"(kProducers) : "memory");
+      if (t < Mr) {
+        float tot = gsum[t];
+        for (int sub = 1; sub < 16 / Mp; ++sub) tot = __fadd_rn(tot, gsum[sub * Mp + t]);
+        for (int c = 0; c < S; ++c) tc::st_cluster_f32(tc::mapa(smem_addr(&part[rank][t]), (uint32_t)c), tot);
+      }
+    } else if (!failed) {
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         float v = __fadd_rn(acc[u].x, acc[u].y);
