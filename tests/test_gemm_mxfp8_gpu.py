@@ -53,7 +53,11 @@ def _dequant(codes, scales, rows, K):
                                    # then the first M of the tiled kernel
                                    (1, 5120, 5120), (8, 1024, 2048), (32, 384, 7168),
                                    (17, 256, 512), (4, 128, 1024), (5, 5120, 7168),
-                                   (2, 256, 384), (33, 256, 1024)])
+                                   (2, 256, 384), (33, 256, 1024),
+                                   # up to 128 rows when N leaves SMs idle: 128-row batch
+                                   # boxes, 2-4 ranks
+                                   (64, 5120, 5120), (100, 1024, 2048), (128, 384, 7168),
+                                   (127, 7168, 1024)])
 def test_mxfp8_gemm_matches_dequantized_product(M, N, K):
     qa, sa, qb, sb = _operands(M, N, K, seed=M + N + K)
     d = mxfp8_gemm(qa, sa, qb, sb)
@@ -69,7 +73,7 @@ def test_mxfp8_gemm_matches_dequantized_product(M, N, K):
 
 
 @pytest.mark.parametrize("M,N,K", [(256, 256, 1024), (1000, 512, 7168), (4736, 8192, 1024),
-                                   (8, 5120, 5120), (32, 1024, 4096)])
+                                   (8, 5120, 5120), (32, 1024, 4096), (128, 5120, 5120)])
 def test_mxfp8_gemm_matches_cublas(M, N, K):
     qa, sa, qb, sb = _operands(M, N, K, seed=7 * M + K)
     d = mxfp8_gemm(qa, sa, qb, sb)
@@ -99,7 +103,7 @@ def test_mxfp8_gemm_empty_and_errors():
     assert _lib.device_error(clear=True) == 0
 
 
-@pytest.mark.parametrize("M,N,K", [(8, 5120, 5120), (32, 1024, 7168)])
+@pytest.mark.parametrize("M,N,K", [(8, 5120, 5120), (32, 1024, 7168), (100, 5120, 5120)])
 def test_mxfp8_gemm_decode_split_is_deterministic(M, N, K):
     """The split-K ranks are added in rank order: repeated calls agree bit for bit."""
     qa, sa, qb, sb = _operands(M, N, K, seed=3 * M + N)

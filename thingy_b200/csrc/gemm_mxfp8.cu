@@ -32,8 +32,9 @@
 //    (tcgen05.ld 32x32b, 32 columns at a time), rounds to bf16 and stores.
 // Tensor memory: the BN accumulator columns, then the scale columns of the 4
 // stages (256 or 512 columns allocated by warp 2, freed by it at the end).
-// No cluster, no multicast. Batches of at most 32 rows take the decode kernel
-// below instead (swapped operands, K split over a cluster).
+// No cluster, no multicast. Batches of at most 32 rows, and of at most 128
+// when N leaves SMs idle, take the decode kernel below instead (swapped
+// operands, K split over a cluster).
 //
 // Every wait is bounded (kWaitLimitCycles): a wait that gives up sets the
 // CTA's abort flag and the device error word; the producer stops issuing and
@@ -222,45 +223,62 @@ __global__ void __launch_bounds__(kThreads, 1)
 
 // ---------------------------------------------------------------- decode
 //
-// Batches of at most 32 rows: the weight is the 128-row M side of the MMA and
-// the batch the 32-wide N side (D^T = B A^T), so a CTA streams 16 KB of
-// weight a K block with a 4 KB batch box (rows past M zero-filled) instead of
-// a 16 KB A box that is nearly all zero. The grid has only N / 128 tiles, so
+// Batches of at most 128 rows: the weight is the 128-row M side of the MMA
+// and the batch the BR-wide N side (D^T = B A^T; BR = 32 up to 32 rows, else
+// 128), so a CTA streams 16 KB of weight a K block with a batch box of BR rows
+// (rows past M zero-filled): up to 32 rows, 4 KB instead of a 16 KB A box
+// that is nearly all zero. The grid has only N / 128 tiles, so
 // K is split over a cluster of S CTAs (grid z) to put more SMs on the weight
-// stream; every rank accumulates its K range in its own tensor memory, the
-// non-leader ranks store their partial tiles into the leader's shared memory
-// (distributed shared memory, no multicast), and the leader adds them in rank
-// order, so the result does not depend on timing. Three K blocks share one
+// stream; every rank accumulates its K range in its own tensor memory and
+// keeps its partial tile in its own shared memory, and each rank then adds
+// the partials of its share of the batch rows over distributed shared memory
+// (no multicast) in rank order, so the result does not depend on timing. Three K blocks share one
 // ring stage and one pair of barriers: at decode sizes the per-stage
 // hand-off, not the bytes, set the time of one-block stages.
-constexpr int kDecodeRows = 32;  // batch rows an MMA covers (its N)
-constexpr int kDecodeStages = 3;
-constexpr int kDecodeBlocks = 3;  // K blocks a stage
-constexpr int kDecodeMaxSplit = 8;
+constexpr int kDecodeRows = 32;     // batch rows of the narrow plan (the MMA's N)
+constexpr int kDecodeWideRows = 128;  // and of the wide one
+constexpr int kDecodeMaxRanks = 8;    // a portable cluster
 
+__device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
+  float4 v;
+  asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
+  return v;
+}
+
+template <int BR>
 struct DecodePlan {
-  static constexpr uint32_t kOffA = kTileBytes;  // batch box: 32 rows x 128 bytes
-  static constexpr uint32_t kOffSfW = kOffA + kDecodeRows * kBK;
+  static constexpr int kStages = 3;
+  static constexpr int kBlocks = BR == kDecodeRows ? 3 : 2;  // K blocks a stage
+  static constexpr uint32_t kOffA = kTileBytes;  // batch box: BR rows x 128 bytes
+  static constexpr uint32_t kOffSfW = kOffA + BR * kBK;
   static constexpr uint32_t kOffSfA = kOffSfW + kSfBytes;
-  static constexpr uint32_t kBlockBytes = (kOffSfA + kSfBytes + 1023u) & ~1023u;  // 21 KB
-  static constexpr uint32_t kStageBytes = kDecodeBlocks * kBlockBytes;
-  static constexpr size_t kSmemBytes = kDecodeStages * kStageBytes + 1024;
-  static constexpr uint32_t kTxBytes = kTileBytes + kDecodeRows * kBK + 2 * kSfBytes;
-  // tensor memory: 32 accumulator columns, then 8 scale columns a block slot
-  static constexpr uint32_t kSfCol = kDecodeRows;
-  static constexpr uint32_t kTmemCols = 128;
-  // the leader's partial-tile buffer (after the ring is idle): [S - 1][32][128] fp32
-  static constexpr uint32_t kPartBytes = kDecodeRows * kBM * 4;
-  static_assert(kSfCol + 8 * kDecodeStages * kDecodeBlocks <= kTmemCols, "tensor memory columns");
-  static_assert((kDecodeMaxSplit - 1) * kPartBytes <= kDecodeStages * kStageBytes, "partials");
+  static constexpr uint32_t kBlockBytes = (kOffSfA + kSfBytes + 1023u) & ~1023u;  // 21 or 33 KB
+  static constexpr uint32_t kStageBytes = kBlocks * kBlockBytes;
+  static constexpr size_t kSmemBytes = kStages * kStageBytes + 1024;
+  static constexpr uint32_t kTxBytes = kTileBytes + BR * kBK + 2 * kSfBytes;
+  // tensor memory: BR accumulator columns, then 8 scale columns a block slot
+  static constexpr uint32_t kSfCol = BR;
+  static constexpr uint32_t kTmemCols = BR + 8 * kStages * kBlocks <= 128 ? 128 : 256;
+  // a rank's partial tile (in its idle ring after the K loop): 128 weight
+  // rows of BR fp32 batch columns, rows kRowStride floats apart
+  static constexpr uint32_t kRowStride = BR + 4;
+  static constexpr uint32_t kPartBytes = kBM * kRowStride * 4;
+  static constexpr int kMaxSplit = kDecodeMaxRanks;
+  static_assert(kSfCol + 8 * kStages * kBlocks <= kTmemCols, "tensor memory columns");
+  static_assert(kPartBytes <= kStages * kStageBytes, "the partial tile fits the ring");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
 };
 
+template <int BR>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_mxfp8_decode_kernel(const __grid_constant__ CUtensorMap map_a,
                              const __grid_constant__ CUtensorMap map_b, const uint8_t* sfa,
                              const uint8_t* sfb, uint16_t* d, int64_t ldd, int M, int K) {
-  using P = DecodePlan;
+  using P = DecodePlan<BR>;
+  constexpr int kDecodeStages = P::kStages;
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t full_bar[kDecodeStages];
   __shared__ __align__(8) uint64_t empty_bar[kDecodeStages];
@@ -276,7 +294,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int KB = K / kBK, S = (int)gridDim.z;
   const uint32_t rank = tc::cluster_ctarank();  // = blockIdx.z: the cluster spans z
   const int kb0 = (int)((int64_t)KB * rank / S), kb1 = (int)((int64_t)KB * (rank + 1) / S);
-  const int NS = (kb1 - kb0 + kDecodeBlocks - 1) / kDecodeBlocks;  // ring stages used
+  const int NS = (kb1 - kb0 + P::kBlocks - 1) / P::kBlocks;  // ring stages used
   volatile uint32_t* abortp = &abort_flag;
 
   if (threadIdx.x == 0) {
@@ -306,7 +324,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t use = (uint32_t)(j / kDecodeStages);
       if (use > 0 && !wait_or_abort(smem_addr(&empty_bar[s]), (use - 1u) & 1u, abortp)) break;
       const uint32_t bar = smem_addr(&full_bar[s]);
-      const int first = kb0 + j * kDecodeBlocks, nb = min(kDecodeBlocks, kb1 - first);
+      const int first = kb0 + j * P::kBlocks, nb = min(P::kBlocks, kb1 - first);
       issued[s] = use + 1u;
       mbar_arrive_expect_tx(bar, (uint32_t)nb * P::kTxBytes);
       for (int i = 0; i < nb; ++i) {
@@ -325,10 +343,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t use = (uint32_t)(j / kDecodeStages);
       if (!wait_or_abort(smem_addr(&full_bar[s]), use & 1u, abortp)) break;
       tc::fence_after();
-      const int first = kb0 + j * kDecodeBlocks, nb = min(kDecodeBlocks, kb1 - first);
+      const int first = kb0 + j * P::kBlocks, nb = min(P::kBlocks, kb1 - first);
       for (int i = 0; i < nb; ++i) {
         const uint32_t st = base + (uint32_t)s * P::kStageBytes + (uint32_t)i * P::kBlockBytes;
-        const uint32_t sfw_col = tmem + P::kSfCol + 8u * (uint32_t)(s * kDecodeBlocks + i);
+        const uint32_t sfw_col = tmem + P::kSfCol + 8u * (uint32_t)(s * P::kBlocks + i);
         const uint32_t sfa_col = sfw_col + 4u;
         tc::copy_sf(sfw_col, smem_desc(st + P::kOffSfW, 0, 128, kLayoutNone));
         tc::copy_sf(sfa_col, smem_desc(st + P::kOffSfA, 0, 128, kLayoutNone));
@@ -336,7 +354,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kk = 0; kk < kBK / 32; ++kk) {
           const uint64_t wd = smem_desc(st + 32u * kk, 16, 1024, kLayoutSw128);
           const uint64_t ad = smem_desc(st + P::kOffA + 32u * kk, 16, 1024, kLayoutSw128);
-          tc::mma_mxf8(tmem, wd, ad, tc::mxf8_idesc(kBM, kDecodeRows, (uint32_t)kk), sfw_col,
+          tc::mma_mxf8(tmem, wd, ad, tc::mxf8_idesc(kBM, BR, (uint32_t)kk), sfw_col,
                        sfa_col, (j | i | kk) != 0);
         }
       }
@@ -353,8 +371,6 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                   *abortp == 0u);
   if (!acc_ok) *abortp = 1u;
   tc::fence_after();
-  uint32_t r[kDecodeRows];
-  if (acc_ok) tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16), r);
   __syncthreads();
   const bool ok = *abortp == 0u;  // the same in every thread after the barrier
   if (!ok) {
@@ -367,63 +383,87 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncthreads();
   }
-  // every rank's ring is idle past this barrier; the leader's becomes the
-  // partial-tile buffer [S - 1][32 batch rows][128 weight rows] fp32
-  tc::cluster_sync();
+  // Reduce-scatter over the cluster. Every rank stores its partial tile into
+  // its own (idle) ring as [M batch rows][128 weight rows] fp32; after a
+  // cluster barrier rank q adds, for the batch rows it owns (a contiguous
+  // share of the M), the S partials in rank order, reading the others over
+  // distributed shared memory, and stores D; a second barrier keeps every
+  // rank's memory until the others are done reading it. A rank that gave up
+  // marks every rank's peer_bad first, so that none stores.
   const int row = warp * 32 + lane;
-  if (rank != 0) {
-    if (ok) {
-      const uint32_t dst = tc::mapa(base, 0) + (rank - 1u) * P::kPartBytes + (uint32_t)row * 4u;
+  const uint32_t tm_row = tmem + ((uint32_t)(warp * 32) << 16);
+  // weight row `row` keeps its batch columns contiguous, rows 16 bytes more
+  // than BR floats apart (16-byte vector stores and loads, at most 4-way bank
+  // conflicts)
+  const uint32_t prow = base + (uint32_t)row * P::kRowStride * 4u;
+  if (ok) {
+    for (int c = 0; c < BR && c < M; c += 32) {
+      uint32_t r[32];
+      tc::tmem_ld32(tm_row + (uint32_t)c, r);
 #pragma unroll
-      for (int m = 0; m < kDecodeRows; ++m)
-        if (m < M) tc::st_cluster_f32(dst + (uint32_t)(m * kBM * 4), __uint_as_float(r[m]));
-    } else if (threadIdx.x == 0) {
-      tc::st_cluster_f32(tc::mapa(smem_addr(&peer_bad), 0), 1.f);
+      for (int k = 0; k < 8; ++k)
+        if (c + 4 * k < M) {
+          const uint32_t v4[4] = {r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]};
+          st_smem(prow + (uint32_t)(c + 4 * k) * 4u, v4);
+        }
     }
+  } else if (threadIdx.x == 0) {
+    for (int q = 0; q < S; ++q) tc::st_cluster_f32(tc::mapa(smem_addr(&peer_bad), (uint32_t)q), 1.f);
   }
-  tc::cluster_sync();
-  if (rank == 0 && ok && peer_bad == 0.f) {
-    const float* part = reinterpret_cast<const float*>(smem_raw + (base - smem_addr(smem_raw)));
+  tc::cluster_sync();  // every partial is in its rank's memory
+  if (peer_bad == 0.f) {
+    // this rank's share of the batch rows, a multiple of 4
+    const int share = ((M + S - 1) / S + 3) & ~3, m_lo = (int)rank * share;
+    const int m_hi = m_lo + share < M ? m_lo + share : M;
     uint16_t* dp = d + n0 + row;
-#pragma unroll
-    for (int m = 0; m < kDecodeRows; ++m) {
-      if (m < M) {
-        float v = __uint_as_float(r[m]);
-        for (int q = 1; q < S; ++q)  // rank order: the sum does not depend on timing
-          v += part[(q - 1) * (kDecodeRows * kBM) + m * kBM + row];
-        dp[(int64_t)m * ldd] = (uint16_t)(f2_to_bf2(make_float2(v, 0.f)) & 0xffffu);
+#pragma unroll 2
+    for (int m4 = m_lo; m4 < m_hi; m4 += 4) {
+      const uint32_t off = prow + (uint32_t)m4 * 4u;
+      float4 acc = ld_cluster_f4(tc::mapa(off, 0u));
+      for (int q = 1; q < S; ++q) {  // rank order: the sum does not depend on timing
+        const float4 o = ld_cluster_f4(tc::mapa(off, (uint32_t)q));
+        acc.x += o.x, acc.y += o.y, acc.z += o.z, acc.w += o.w;
       }
+      const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e)
+        if (m4 + e < m_hi)
+          dp[(int64_t)(m4 + e) * ldd] = (uint16_t)(f2_to_bf2(make_float2(v[e], 0.f)) & 0xffffu);
     }
-  }
-  if (rank == 0 && threadIdx.x == 0 && peer_bad != 0.f)
+  } else if (threadIdx.x == 0) {
     atomicCAS(&g_gemm_device_error, kDevErrNone, kDevErrBulkWaitTimeout);
+  }
+  tc::cluster_sync();  // the others are done reading this rank's partial
   tc::fence_before();
   __syncthreads();
   if (warp == 2) tc::tmem_dealloc(tmem, P::kTmemCols);
 }
 
-// Ranks a tile's K range is split over: enough CTAs for the SMs, at most 8 (a
-// portable cluster), at least one K block a rank.
-int decode_splits(int64_t N, int64_t K) {
+// Ranks a tile's K range is split over: enough CTAs for the SMs, at most
+// max_split (the partial tiles fit the leader's ring; 8 at most, a portable
+// cluster), at least one K block a rank.
+int decode_splits(int64_t N, int64_t K, int max_split) {
   const int64_t tiles = N / kBM, kb = K / kBK;
   int64_t s = device_sm_count() / tiles;
-  if (s > kDecodeMaxSplit) s = kDecodeMaxSplit;
+  if (s > max_split) s = max_split;
   if (s > kb) s = kb;
   return s < 1 ? 1 : (int)s;
 }
 
+template <int BR>
 cudaError_t launch_decode(const CUtensorMap& map_a, const CUtensorMap& map_b, const void* a_scale,
                           const void* b_scale, void* d, int64_t ldd, int64_t M, int64_t N,
                           int64_t K, cudaStream_t stream) {
-  auto kernel = gemm_mxfp8_decode_kernel;
+  using P = DecodePlan<BR>;
+  auto kernel = gemm_mxfp8_decode_kernel<BR>;
   const cudaError_t e = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                             (int)DecodePlan::kSmemBytes);
+                                             (int)P::kSmemBytes);
   if (e != cudaSuccess) return e;
-  const int S = decode_splits(N, K);
+  const int S = decode_splits(N, K, P::kMaxSplit);
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3((unsigned)(N / kBM), 1, (unsigned)S);
   cfg.blockDim = dim3(kThreads);
-  cfg.dynamicSmemBytes = DecodePlan::kSmemBytes;
+  cfg.dynamicSmemBytes = P::kSmemBytes;
   cfg.stream = stream;
   cudaLaunchAttribute attr[2];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
@@ -481,9 +521,15 @@ cudaError_t device_error_gemm(int* out, bool clear) {
 int gemm_mxfp8(const void* a, int64_t lda, const void* a_scale, const void* b, int64_t ldb,
                const void* b_scale, void* d, int64_t ldd, int64_t M, int64_t N, int64_t K,
                cudaStream_t stream, const char** why) {
-  const bool decode = M <= kDecodeRows;
+  // decode plans: up to 32 rows, and up to 128 rows when the 128-wide tiles
+  // leave SMs for a K split of at least 2
+  const int box_rows = M <= kDecodeRows ? kDecodeRows : kDecodeWideRows;
+  const bool decode =
+      M <= kDecodeRows ||
+      (M <= kDecodeWideRows &&
+       decode_splits(N, K, DecodePlan<kDecodeWideRows>::kMaxSplit) >= 2);
   CUtensorMap map_a, map_b;
-  if (!tc::encode_e4m3_operand(&map_a, a, M, K, lda, decode ? kDecodeRows : kBM) ||
+  if (!tc::encode_e4m3_operand(&map_a, a, M, K, lda, decode ? box_rows : kBM) ||
       !tc::encode_e4m3_operand(&map_b, b, N, K, ldb)) {
     *why = "cuTensorMapEncodeTiled failed for an operand";
     return CUTIE_ERR_CUDA;
@@ -493,7 +539,11 @@ int gemm_mxfp8(const void* a, int64_t lda, const void* a_scale, const void* b, i
   // give every SM one, else 128-wide tiles, twice as many CTAs
   const bool wide = N % 256 == 0 && (N / 256) * ((M + kBM - 1) / kBM) >= device_sm_count();
   const cudaError_t e =
-      decode ? launch_decode(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K, stream)
+      decode ? (M <= kDecodeRows
+                    ? launch_decode<kDecodeRows>(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K,
+                                                 stream)
+                    : launch_decode<kDecodeWideRows>(map_a, map_b, a_scale, b_scale, d, ldd, M,
+                                                     N, K, stream))
       : wide ? launch_gemm<256>(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K, stream)
              : launch_gemm<128>(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K, stream);
   if (e != cudaSuccess) {
