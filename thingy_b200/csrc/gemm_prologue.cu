@@ -591,37 +591,50 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   if constexpr (SM) {
     // D^T in tensor memory: warp w (< 4) holds weight rows n0 + 32 w + lane,
-    // one column a block row. Once every CTA's MMAs are done the others store
-    // their Mr columns into the leader's x region ([S - 1][Mr][128] fp32);
-    // the leader adds them to its own in rank order and stores D.
+    // one column a block row. Reduce-scatter over the cluster: every CTA
+    // stores its partial tile into its own (idle) x region, weight row n at
+    // 80 n bytes with its Mr columns contiguous; after a cluster barrier CTA q
+    // adds, for its share of the block rows, the S partials in rank order
+    // (16-byte distributed shared memory loads) and stores D; a second barrier
+    // keeps every CTA's memory until the others are done reading it.
+    constexpr uint32_t kRowBytes = (16 + 4) * 4;
+    static_assert(kTM * kRowBytes <= P::kXRegion, "the partial tile fits the x region");
     const int n = warp * 32 + lane;  // weight row of the tile = column of D
-    uint32_t r[32];
-    if (acc_ok) tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + kAccCol, r);
-    if (S > 1) {
-      tc::cluster_sync();  // every CTA's MMAs are done: the leader's memory is free
-      if (rank > 0 && acc_ok) {
-        const uint32_t dst =
-            tc::mapa(base + P::kOffX + ((uint32_t)(rank - 1) * (uint32_t)Mr * kTN + (uint32_t)n) * 4u,
-                     0u);
+    const uint32_t prow = base + P::kOffX + (uint32_t)n * kRowBytes;
+    if (acc_ok) {
+      uint32_t r[32];
+      tc::tmem_ld32(tmem + ((uint32_t)(warp * 32) << 16) + kAccCol, r);
 #pragma unroll
-        for (int m = 0; m < 16; ++m)
-          if (m < Mr) tc::st_cluster_f32(dst + (uint32_t)(m * kTN * 4), __uint_as_float(r[m]));
-      }
-      tc::cluster_sync();  // every partial is in place
-    }
-    if ((S == 1 || rank == 0) && acc_ok) {
-      const float* part_t =
-          reinterpret_cast<const float*>(smem_raw + (base + P::kOffX - smem_addr(smem_raw)));
-#pragma unroll
-      for (int m = 0; m < 16; ++m) {
-        if (m < Mr) {
-          float v = __uint_as_float(r[m]);
-          for (int p = 1; p < S; ++p)  // the other CTAs' partials, in rank order
-            v = __fadd_rn(v, part_t[((p - 1) * Mr + m) * kTN + n]);
-          a.d[(m0 + m) * a.ldd + n0 + n] = (uint16_t)(f2_to_bf2(make_float2(v, 0.f)) & 0xffffu);
+      for (int k = 0; k < 4; ++k)
+        if (4 * k < Mr) {
+          const uint32_t v4[4] = {r[4 * k], r[4 * k + 1], r[4 * k + 2], r[4 * k + 3]};
+          st_smem(prow + 16u * (uint32_t)k, v4);
         }
+    }
+    if (S > 1) tc::cluster_sync();  // every partial is in its CTA's memory
+    if (acc_ok) {
+      const int share = ((Mr + S - 1) / S + 3) & ~3, m_lo = rank * share;
+      const int m_hi = m_lo + share < Mr ? m_lo + share : Mr;
+      for (int m4 = m_lo; m4 < m_hi; m4 += 4) {
+        const uint32_t off = prow + (uint32_t)m4 * 4u;
+        uint4 o = ld_cluster_v4(tc::mapa(off, 0u));
+        float v[4] = {__uint_as_float(o.x), __uint_as_float(o.y), __uint_as_float(o.z),
+                      __uint_as_float(o.w)};
+        for (int p = 1; p < S; ++p) {  // the other CTAs' partials, in rank order
+          o = ld_cluster_v4(tc::mapa(off, (uint32_t)p));
+          v[0] = __fadd_rn(v[0], __uint_as_float(o.x));
+          v[1] = __fadd_rn(v[1], __uint_as_float(o.y));
+          v[2] = __fadd_rn(v[2], __uint_as_float(o.z));
+          v[3] = __fadd_rn(v[3], __uint_as_float(o.w));
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e)
+          if (m4 + e < m_hi)
+            a.d[(m0 + m4 + e) * a.ldd + n0 + n] =
+                (uint16_t)(f2_to_bf2(make_float2(v[e], 0.f)) & 0xffffu);
       }
     }
+    if (S > 1) tc::cluster_sync();  // the others are done reading this CTA's partial
   } else {
     const int row = warp * 32 + lane;  // tile row of this thread (warps 0-3)
     const bool row_live = warp < kProducerWarps && row < Mr;
