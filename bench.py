@@ -341,7 +341,7 @@ def device_run(args, w, M, src, device, local_rank, world, K, unfused=False):
                                     scale_format="e8m0", scale_layout="mx")
                 mxfp8_gemm(s.q, s.scale, s.qb, s.sb, out=s.d)
             else:
-                rms_norm_mxfp8_gemm(s.x, weight, w.eps, s.qb, s.sb, out=s.d)
+                rms_norm_mxfp8_gemm(s.x, weight, w.eps, s.qb, s.sb, out=s.d, fused=True)
             return
         if w.kind == "bwd":  # backward: two kernels (rows, then the d_weight reduction)
             launch_rms_norm_backward(

@@ -63,9 +63,11 @@ def mxfp8_gemm(a: torch.Tensor, a_scale: torch.Tensor, b: torch.Tensor, b_scale:
     return out
 
 
-# Rows up to which the fused kernel beats the two-kernel path (measured on a
-# B200 at K = N = 5120: 1.29x at M = 1-8, 1.12x at M = 32, 0.79x at M = 64).
-FUSED_MAX_ROWS = 32
+# Rows up to which the fused kernel is the default (measured on a B200 at
+# K = N = 5120 against the two-kernel path: with eager launches 1.32-1.41x at
+# M = 1-16 and 1.05x at 32; in device time, launches replayed from a CUDA
+# graph, 0.93-0.98x at M = 1-16 and 0.71x at 32).
+FUSED_MAX_ROWS = 16
 
 
 def rms_norm_mxfp8_gemm(x: torch.Tensor, weight: torch.Tensor, eps: float, b: torch.Tensor,
