@@ -224,8 +224,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- decode
 //
 // Batches of at most 128 rows: the weight is the 128-row M side of the MMA
-// and the batch the BR-wide N side (D^T = B A^T; BR = 32 up to 32 rows, else
-// 128), so a CTA streams 16 KB of weight a K block with a batch box of BR rows
+// and the batch the BR-wide N side (D^T = B A^T; BR = 32, 64 or 128: the
+// smallest that holds the batch), so a CTA streams 16 KB of weight a K block with a batch box of BR rows
 // (rows past M zero-filled): up to 32 rows, 4 KB instead of a 16 KB A box
 // that is nearly all zero. The grid has only N / 128 tiles, so
 // K is split over a cluster of S CTAs (grid z) to put more SMs on the weight
@@ -236,6 +236,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ring stage and one pair of barriers: at decode sizes the per-stage
 // hand-off, not the bytes, set the time of one-block stages.
 constexpr int kDecodeRows = 32;     // batch rows of the narrow plan (the MMA's N)
+constexpr int kDecodeMidRows = 64;    // of the middle one
 constexpr int kDecodeWideRows = 128;  // and of the wide one
 constexpr int kDecodeMaxRanks = 8;    // a portable cluster
 
@@ -251,7 +252,7 @@ __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
 template <int BR>
 struct DecodePlan {
   static constexpr int kStages = 3;
-  static constexpr int kBlocks = BR == kDecodeRows ? 3 : 2;  // K blocks a stage
+  static constexpr int kBlocks = BR == kDecodeWideRows ? 2 : 3;  // K blocks a stage
   static constexpr uint32_t kOffA = kTileBytes;  // batch box: BR rows x 128 bytes
   static constexpr uint32_t kOffSfW = kOffA + BR * kBK;
   static constexpr uint32_t kOffSfA = kOffSfW + kSfBytes;
@@ -523,7 +524,8 @@ int gemm_mxfp8(const void* a, int64_t lda, const void* a_scale, const void* b, i
                cudaStream_t stream, const char** why) {
   // decode plans: up to 32 rows, and up to 128 rows when the 128-wide tiles
   // leave SMs for a K split of at least 2
-  const int box_rows = M <= kDecodeRows ? kDecodeRows : kDecodeWideRows;
+  const int box_rows =
+      M <= kDecodeRows ? kDecodeRows : M <= kDecodeMidRows ? kDecodeMidRows : kDecodeWideRows;
   const bool decode =
       M <= kDecodeRows ||
       (M <= kDecodeWideRows &&
@@ -542,6 +544,9 @@ int gemm_mxfp8(const void* a, int64_t lda, const void* a_scale, const void* b, i
       decode ? (M <= kDecodeRows
                     ? launch_decode<kDecodeRows>(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K,
                                                  stream)
+                : M <= kDecodeMidRows
+                    ? launch_decode<kDecodeMidRows>(map_a, map_b, a_scale, b_scale, d, ldd, M, N,
+                                                    K, stream)
                     : launch_decode<kDecodeWideRows>(map_a, map_b, a_scale, b_scale, d, ldd, M,
                                                      N, K, stream))
       : wide ? launch_gemm<256>(map_a, map_b, a_scale, b_scale, d, ldd, M, N, K, stream)
