@@ -420,11 +420,16 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 2
     for (int m4 = m_lo; m4 < m_hi; m4 += 4) {
       const uint32_t off = prow + (uint32_t)m4 * 4u;
-      float4 acc = ld_cluster_f4(tc::mapa(off, 0u));
-      for (int q = 1; q < S; ++q) {  // rank order: the sum does not depend on timing
-        const float4 o = ld_cluster_f4(tc::mapa(off, (uint32_t)q));
-        acc.x += o.x, acc.y += o.y, acc.z += o.z, acc.w += o.w;
-      }
+      // every rank's 16 bytes are requested before the first is added
+      float4 o[kDecodeMaxRanks];
+#pragma unroll
+      for (int q = 0; q < kDecodeMaxRanks; ++q)
+        if (q < S) o[q] = ld_cluster_f4(tc::mapa(off, (uint32_t)q));
+      float4 acc = o[0];
+#pragma unroll
+      for (int q = 1; q < kDecodeMaxRanks; ++q)
+        if (q < S)  // rank order: the sum does not depend on timing
+          acc.x += o[q].x, acc.y += o[q].y, acc.z += o[q].z, acc.w += o[q].w;
       const float v[4] = {acc.x, acc.y, acc.z, acc.w};
 #pragma unroll
       for (int e = 0; e < 4; ++e)
