@@ -617,15 +617,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m_hi = m_lo + share < Mr ? m_lo + share : Mr;
       for (int m4 = m_lo; m4 < m_hi; m4 += 4) {
         const uint32_t off = prow + (uint32_t)m4 * 4u;
-        uint4 o = ld_cluster_v4(tc::mapa(off, 0u));
-        float v[4] = {__uint_as_float(o.x), __uint_as_float(o.y), __uint_as_float(o.z),
-                      __uint_as_float(o.w)};
-        for (int p = 1; p < S; ++p) {  // the other CTAs' partials, in rank order
-          o = ld_cluster_v4(tc::mapa(off, (uint32_t)p));
-          v[0] = __fadd_rn(v[0], __uint_as_float(o.x));
-          v[1] = __fadd_rn(v[1], __uint_as_float(o.y));
-          v[2] = __fadd_rn(v[2], __uint_as_float(o.z));
-          v[3] = __fadd_rn(v[3], __uint_as_float(o.w));
+        // every CTA's 16 bytes are requested before the first is added
+        uint4 o[kMaxSplits];
+#pragma unroll
+        for (int p = 0; p < kMaxSplits; ++p)
+          if (p < S) o[p] = ld_cluster_v4(tc::mapa(off, (uint32_t)p));
+        float v[4] = {__uint_as_float(o[0].x), __uint_as_float(o[0].y), __uint_as_float(o[0].z),
+                      __uint_as_float(o[0].w)};
+#pragma unroll
+        for (int p = 1; p < kMaxSplits; ++p) {
+          if (p < S) {  // the other CTAs' partials, in rank order
+            v[0] = __fadd_rn(v[0], __uint_as_float(o[p].x));
+            v[1] = __fadd_rn(v[1], __uint_as_float(o[p].y));
+            v[2] = __fadd_rn(v[2], __uint_as_float(o[p].z));
+            v[3] = __fadd_rn(v[3], __uint_as_float(o[p].w));
+          }
         }
 #pragma unroll
         for (int e = 0; e < 4; ++e)
