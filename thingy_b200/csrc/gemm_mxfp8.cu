@@ -224,17 +224,21 @@ __global__ void __launch_bounds__(kThreads, 1)
 // ---------------------------------------------------------------- decode
 //
 // Batches of at most 128 rows: the weight is the 128-row M side of the MMA
-// and the batch the BR-wide N side (D^T = B A^T; BR = 32, 64 or 128: the
-// smallest that holds the batch), so a CTA streams 16 KB of weight a K block with a batch box of BR rows
-// (rows past M zero-filled): up to 32 rows, 4 KB instead of a 16 KB A box
-// that is nearly all zero. The grid has only N / 128 tiles, so
-// K is split over a cluster of S CTAs (grid z) to put more SMs on the weight
-// stream; every rank accumulates its K range in its own tensor memory and
-// keeps its partial tile in its own shared memory, and each rank then adds
-// the partials of its share of the batch rows over distributed shared memory
-// (no multicast) in rank order, so the result does not depend on timing. Three K blocks share one
-// ring stage and one pair of barriers: at decode sizes the per-stage
-// hand-off, not the bytes, set the time of one-block stages.
+// and the batch the BR-wide N side (D^T = B A^T; BR = 32, 64 or 128, the
+// smallest that holds the batch), so a CTA streams 16 KB of weight a K block
+// with a batch box of BR rows (rows past M zero-filled): up to 32 rows, 4 KB
+// instead of a 16 KB A box that is nearly all zero.
+//
+// The grid has only N / 128 tiles, so K is split over a cluster of S CTAs
+// (grid z) to put more SMs on the weight stream. Every rank accumulates its
+// K range in its own tensor memory and keeps its partial tile in its own
+// shared memory; each rank then adds, for its share of the batch rows, the
+// partials of all ranks in rank order over distributed shared memory (no
+// multicast), so the result does not depend on timing.
+//
+// Two or three K blocks share one ring stage and one pair of barriers: at
+// decode sizes the per-stage hand-off, not the bytes, set the time of
+// one-block stages.
 constexpr int kDecodeRows = 32;     // batch rows of the narrow plan (the MMA's N)
 constexpr int kDecodeMidRows = 64;    // of the middle one
 constexpr int kDecodeWideRows = 128;  // and of the wide one
