@@ -240,14 +240,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc::fence_after();
   const uint32_t tmem = tmem_slot;
-  tc::cluster_sync();  // every CTA's part[] exists before the others write it
+  // Set-up cluster barrier: every CTA of the cluster has started (its part[]
+  // exists) before another writes it. Each thread arrives here and waits
+  // only before its next cluster barrier or its first remote write, so the
+  // loads into this CTA's own memory do not wait for the other CTAs.
+  tc::cluster_arrive();
   griddep_wait();      // x, w and B written by the previous kernel are complete
   griddep_launch_dependents();
 
   // ---- streaming warps: they arrive on the end-of-pass-1 cluster barrier
-  // first (they have no part in pass 1) and wait on it after streaming
+  // before they could block (they have no part in pass 1) and wait on it
+  // after streaming
   if (warp == kWarpX) {
-    tc::cluster_arrive();
     // x iterations 0 .. kbs-1 feed pass 1, kbs .. 2 kbs-1 pass 2 (a resident
     // ring keeps pass 1's stages for pass 2: kbs iterations). The first XS
     // need no wait; the weight stream starts once they are issued, so that
@@ -273,11 +277,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) issue_x(0, x_first);
     __syncwarp();
     asm volatile("bar.arrive %0, %1;" ::"n"(kBarStreams), "n"(64) : "memory");
+    tc::cluster_wait();     // set-up
+    tc::cluster_arrive();   // end of pass 1
     if (lane == 0) issue_x(x_first, x_iters);
     __syncwarp();
     tc::cluster_wait();
   } else if (warp == kWarpB) {
-    tc::cluster_arrive();
+    tc::cluster_wait();     // set-up
+    tc::cluster_arrive();   // end of pass 1
     asm volatile("bar.sync %0, %1;" ::"n"(kBarStreams), "n"(64) : "memory");
     if (lane == 0) {
       // stage j holds K blocks BG j .. BG j + BG - 1 in slots BG (j % NSB) + ...
@@ -304,7 +311,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     tc::cluster_wait();
   } else if (warp == kWarpMma) {
-    tc::cluster_arrive();  // the MMAs wait for A tiles, which come after pass 1
+    tc::cluster_wait();     // set-up
+    tc::cluster_arrive();   // the MMAs wait for A tiles, which come after pass 1
     tc::cluster_wait();
     if constexpr (SM) {
       // stage j takes weight stage j and A group j (the same three K blocks)
@@ -448,6 +456,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     // one decision for the four warps
     const bool failed = tc::bar_or(kBarProducers, kProducers, lost || *abortp != 0u);
+    tc::cluster_wait();  // set-up: every CTA has started before the partials go out
     // row partials: the 8 lanes of a row add their chunks (a symmetric
     // butterfly: all 8 get the same bits), then lane j of the row writes it
     // into part[rank][row] of CTA j (and j + 8) of the cluster
