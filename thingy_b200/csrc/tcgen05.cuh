@@ -89,16 +89,6 @@ __device__ __forceinline__ void commit(uint32_t bar) {
                : "memory");
 }
 
-// The same arrival on the mbarrier at offset `bar` of every CTA of the
-// cluster named in `cta_mask`.
-__device__ __forceinline__ void commit_multicast(uint32_t bar, uint16_t cta_mask) {
-  asm volatile(
-      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
-      " [%0], %1;" ::"r"(bar),
-      "h"(cta_mask)
-      : "memory");
-}
-
 __device__ __forceinline__ void tmem_alloc(uint32_t slot_smem, uint32_t cols) {
   asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(slot_smem),
                "r"(cols)
